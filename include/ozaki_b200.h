@@ -1,0 +1,187 @@
+/*
+ * ozaki_b200.h -- C ABI of libozaki_b200.so, the B200 (sm_100a) kernels behind
+ * the Ozaki FP64-emulation matmul path of Efithor/ozaki-jax.
+ *
+ * The reference runs this path as jitted JAX/XLA (or Pallas-TPU) operators
+ * with static integer arguments and device FP64 arrays in and out.  Each entry
+ * point below replaces one of them; the comment on each names the reference
+ * function (file:line, paths inside the reference project) it stands in for.
+ *
+ * Conventions
+ *   - All matrices are row-major (C order, as NumPy and JAX use); `ld*` are
+ *     leading dimensions in elements.  Pointers to matrices are DEVICE pointers.
+ *   - Calls are asynchronous and ordered on `stream` (a cudaStream_t passed as
+ *     void*; NULL = legacy default stream).  Nothing is synchronised inside
+ *     a call unless its comment says so.
+ *   - Return value: OZK_OK (0) when the work was validated and enqueued, or a
+ *     negative ozk_status.  Conditions found by a kernel (non-finite input, a
+ *     device-side wait that ran out of time) are OR-ed as OZK_FLAG_* bits into
+ *     the caller's device word `status_dev` (int32, may be NULL to skip); read
+ *     it after the stream completes, or call ozk_check_status().
+ *   - Slices are BF16 bit patterns (uint16); exponents are int32.
+ *   - No C++ exceptions cross this boundary; no global mutable state other
+ *     than per-device caches created on first use.
+ */
+#ifndef OZAKI_B200_H
+#define OZAKI_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  OZK_OK = 0,
+  OZK_ERR_ARG = -1,         /* invalid argument (shape, mode, pointer, size) */
+  OZK_ERR_UNSAFE = -2,      /* preflight bound violated (bits <= 0, K bound) */
+  OZK_ERR_NONFINITE = -3,   /* an input holds NaN/Inf or overflows FP32 */
+  OZK_ERR_CUDA = -4,        /* a CUDA runtime/driver call failed */
+  OZK_ERR_NCCL = -5,        /* a collective failed */
+  OZK_ERR_TIMEOUT = -6,     /* a device-side wait exceeded its time budget */
+  OZK_ERR_WORKSPACE = -7,   /* caller workspace too small */
+  OZK_ERR_UNSUPPORTED = -8  /* valid request this build does not handle */
+} ozk_status;
+
+/* Bits OR-ed into *status_dev by kernels. */
+#define OZK_FLAG_NONFINITE 0x1  /* non-finite value seen while splitting */
+#define OZK_FLAG_TIMEOUT 0x2    /* a bounded device wait gave up */
+#define OZK_FLAG_RANGE 0x4      /* a finite FP64 input overflows FP32 when split */
+
+/* Accumulation modes of ozk_slice_gemm. */
+#define OZK_ACC_F64 0       /* FP64 running sum in the GEMM epilogue -> C (double) */
+#define OZK_ACC_PRODUCTS 1  /* write each pair's exact FP32 product -> products */
+
+/* ---------------------------------------------------------------- policies */
+
+/* _compute_rho_f32 (ozaki_jax/extract.py:109-113). */
+int ozk_compute_rho_f32(int64_t K);
+/* _compute_rho (ozaki_jax/extract.py:12-18), FP64 host pipeline. */
+int ozk_compute_rho_f64(int64_t K);
+/* _make_pair_schedule (ozaki_jax/pallas_gemm_accum.py:26-87): writes the
+ * slice-pair order (hi x hi, hi x lo, lo x hi) into pair_a/pair_b (capacity
+ * `cap`) and returns the pair count, or OZK_ERR_ARG. */
+int ozk_pair_schedule(int n_hi, int n_lo, uint8_t* pair_a, uint8_t* pair_b, int cap);
+/* Host-pipeline triangular schedule i + j <= n-1 (ozaki_jax/matmul.py:23-32). */
+int ozk_triangular_schedule(int n_slices, uint8_t* pair_a, uint8_t* pair_b, int cap);
+
+/* ---------------------------------------------------------------- kernels */
+
+/* Row extraction of an FP64 matrix X (rows x K, ldx): double-FP32 split
+ * (_jax_double_f32_split, ozaki_jax/matmul.py:204-213) followed by n_hi
+ * sigma-trick slices of the hi part and n_lo of the lo part
+ * (jax_extract_split_rows, ozaki_jax/extract.py:197-242), bit-identical to the
+ * reference.  slices: [n_hi+n_lo][rows][k_pad] BF16 (k_pad >= K, multiple of
+ * 64; columns K..k_pad-1 are written as zeros); exps: [n_hi+n_lo][rows]. */
+int ozk_extract_rows_f64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                         int n_hi, int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                         int32_t* status_dev, void* stream);
+
+/* Column extraction of X (K x cols, ldx) (jax_extract_split_cols,
+ * ozaki_jax/extract.py:245-286), written transposed: slices
+ * [n_hi+n_lo][cols][k_pad] (K contiguous), exps [n_hi+n_lo][cols]. */
+int ozk_extract_cols_f64(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho,
+                         int n_hi, int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                         int32_t* status_dev, void* stream);
+
+/* FP64 sigma-trick extraction of the host pipeline (extract_split_rows /
+ * extract_split_cols, ozaki_jax/extract.py:21-103): n_slices slices of the
+ * FP64 input itself, same layouts as above. */
+int ozk_extract_rows_host_f64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                              int n_slices, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                              int32_t* status_dev, void* stream);
+int ozk_extract_cols_host_f64(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho,
+                              int n_slices, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                              int32_t* status_dev, void* stream);
+
+/* Persistent tcgen05/TMEM slice-pair GEMM over a pair list, replacing the
+ * slice GEMMs and the scaled 2Sum accumulation of the reference
+ * (ozaki_jax/matmul.py:248-281, :418-488; ozaki_jax/pallas_ops.py:178-239;
+ * the fused Pallas kernel ozaki_jax/pallas_gemm_accum.py:90-316).
+ *   SA: [nA][N][k_pad] BF16 left slices, eA: [nA][N];
+ *   SB: [nB][M][k_pad] BF16 right slices (K contiguous), eB: [nB][M].
+ *   Pair p multiplies SA[pair_a[p]] by SB[pair_b[p]]^T; pair_a/pair_b are
+ *   HOST arrays of n_pairs (<= 128) entries.
+ * mode OZK_ACC_F64:  C[r][c] = beta*Cin[r][c] + alpha * sum_p P_p[r][c]
+ *                    * 2^(eA[a][r] + eB[b][c]), summed in FP64 in pair order
+ *                    (Cin may be NULL when beta == 0).
+ * mode OZK_ACC_PRODUCTS: products[p][r][c] = P_p[r][c] (FP32, exact), ld = M.
+ * symmetric != 0 (gram): requires SA == SB, eA == eB, N == M; only tiles on
+ * or above the diagonal are computed and each is also written mirrored, so C
+ * is exactly symmetric. */
+int ozk_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t* SB,
+                   const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
+                   const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
+                   int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
+                   double* C, int64_t ldc, float* products, int32_t* status_dev, void* stream);
+
+/* Reference-order FP32 2Sum accumulation of materialised products
+ * (accumulate_2sum / _accumulate_2sum_logic, ozaki_jax/pallas_ops.py:178-239,
+ * :372-396, with the scales of _precompute_accumulation_scales, :107-175):
+ * products [n_pairs][N][M] in ondevice_pairs(n_hi, n_lo) order; writes
+ * C_hi, C_lo (FP32, may be NULL) and C = f64(C_hi) + f64(C_lo) (may be NULL).
+ * Bit-identical to the reference's fused / ondevice accumulation. */
+int ozk_accumulate_2sum(const float* products, const int32_t* eA, const int32_t* eB,
+                        int64_t N, int64_t M, int n_hi, int n_lo, float* C_hi, float* C_lo,
+                        double* C, int64_t ldc, void* stream);
+
+/* ---------------------------------------------------------------- pipelines */
+
+/* Workspace bytes ozk_matmul_f64 needs for an N x K by K x M product with
+ * (n_hi, n_lo) slices. */
+size_t ozk_matmul_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo);
+
+/* The on-device pipeline (_matmul_ondevice accumulation='fused' /
+ * 'bf16_interleaved' -> _fully_fused_f64_jit / _bf16_interleaved_f64_jit,
+ * ozaki_jax/matmul.py:514-540, :641-686): C = A @ B with FP64 inputs and
+ * output on the device.  rho < 0 selects _compute_rho_f32(K).  workspace may be
+ * NULL (then it is taken from the stream-ordered pool and returned).
+ * acc_mode: OZK_ACC_F64 (FP64 epilogue) or OZK_ACC_PRODUCTS (materialised
+ * products + reference 2Sum, bit-identical to the reference's result). */
+int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
+                   int64_t ldc, int64_t N, int64_t K, int64_t M, int rho, int n_hi, int n_lo,
+                   int acc_mode, void* workspace, size_t ws_bytes, int32_t* status_dev,
+                   void* stream);
+
+/* The FP64 host pipeline (matmul(pipeline='host'), ozaki_jax/matmul.py:823-851):
+ * FP64 extraction into n_slices slices, triangular pairs, FP64 accumulation,
+ * all on the device.  rho < 0 selects _compute_rho(K). */
+size_t ozk_matmul_host_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_slices);
+int ozk_matmul_host_f64(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
+                        int64_t ldc, int64_t N, int64_t K, int64_t M, int rho, int n_slices,
+                        void* workspace, size_t ws_bytes, int32_t* status_dev, void* stream);
+
+/* gram(mode='ozaki') (_gram_ozaki_jit, ozaki_jax/gram.py:19-37): G = A^T A for
+ * A (N x K, lda), G (K x K, ldg), rho < 0 selects _compute_rho_f32(N).  The
+ * slices of A are extracted once and serve both operands. */
+size_t ozk_gram_workspace_bytes(int64_t N, int64_t K, int n_hi, int n_lo);
+int ozk_gram_f64(const double* A, int64_t lda, double* G, int64_t ldg, int64_t N, int64_t K,
+                 int rho, int n_hi, int n_lo, void* workspace, size_t ws_bytes,
+                 int32_t* status_dev, void* stream);
+
+/* residual(mode='ozaki') (_residual_ozaki_jit / _ozaki_matvec_f64,
+ * ozaki_jax/solve.py:38-53, :78-82): R = Bv - A @ X for A (N x K), X (K x M),
+ * Bv and R (N x M).  rho < 0 selects _compute_rho_f32(K). */
+size_t ozk_residual_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo);
+int ozk_residual_f64(const double* A, int64_t lda, const double* X, int64_t ldx,
+                     const double* Bv, int64_t ldb, double* R, int64_t ldr, int64_t N,
+                     int64_t K, int64_t M, int rho, int n_hi, int n_lo, void* workspace,
+                     size_t ws_bytes, int32_t* status_dev, void* stream);
+
+/* ---------------------------------------------------------------- status */
+
+/* Synchronises `stream`, reads *status_dev (device) and returns OZK_OK,
+ * OZK_ERR_NONFINITE or OZK_ERR_TIMEOUT (timeout wins), or OZK_ERR_CUDA. */
+int ozk_check_status(const int32_t* status_dev, void* stream);
+/* Static text for a status code. */
+const char* ozk_strerror(int status);
+/* Copies the last error detail of the calling host thread into buf. */
+int ozk_last_error_detail(char* buf, size_t len);
+/* Library version string. */
+const char* ozk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OZAKI_B200_H */

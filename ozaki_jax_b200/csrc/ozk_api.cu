@@ -1,0 +1,410 @@
+// extern "C" entry points of libozaki_b200.so (declared in ozaki_b200.h):
+// argument validation, the reference's policies (rho, presets, pair
+// schedules, preflight bounds), workspace layout and kernel sequencing.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "ozaki_b200.h"
+#include "ozk_internal.h"
+
+namespace ozk {
+
+static thread_local char t_detail[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_detail, sizeof(t_detail), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int set_cuda_error(const char* what, cudaError_t e) {
+  return set_error(OZK_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int device_sm_count(int dev) {
+  static int cache[64] = {0};
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+// Time budget of every device-side wait (default 2 s; OZK_WAIT_BUDGET_MS
+// overrides it).  A legitimate wait lasts microseconds.
+uint64_t wait_budget_ns() {
+  static uint64_t v = 0;
+  if (!v) {
+    const char* s = getenv("OZK_WAIT_BUDGET_MS");
+    long ms = s ? atol(s) : 0;
+    v = (uint64_t)(ms > 0 ? ms : 2000) * 1000000ull;
+  }
+  return v;
+}
+
+static int rho_f32(int64_t K) {  // extract.py:109-113
+  int64_t k = K < 2 ? 2 : K;
+  int lg = 0;
+  while (((int64_t)1 << lg) < k) ++lg;  // ceil(log2 k)
+  int gamma = (int)ceil(24.0 - (24.0 - lg) / 2.0);
+  return gamma > 17 ? gamma : 17;
+}
+
+static int rho_f64(int64_t K) {  // extract.py:12-18
+  int64_t k = K < 2 ? 2 : K;
+  int lg = 0;
+  while (((int64_t)1 << lg) < k) ++lg;
+  int gamma = (int)ceil(53.0 - (24.0 - lg) / 2.0);
+  return gamma > 46 ? gamma : 46;
+}
+
+// BF16 -> FP32 exact inner-product bound K * (2^bits - 1)^2 < 2^24
+// (matmul.py:605-621 and :84-97).
+static int check_bound(int64_t K, int bits) {
+  if (bits <= 0)
+    return set_error(OZK_ERR_UNSAFE, "non-positive bits per slice (%d); K=%lld is too large", bits,
+                     (long long)K);
+  double m = (double)(((int64_t)1 << bits) - 1);
+  if ((double)K * m * m >= 16777216.0)
+    return set_error(OZK_ERR_UNSAFE, "K=%lld violates BF16->FP32 exact inner-product bound",
+                     (long long)K);
+  return OZK_OK;
+}
+
+static int ondevice_pairs(int n_hi, int n_lo, uint8_t* pa, uint8_t* pb, int cap) {
+  if (n_hi < 1 || n_lo < 0 || n_hi > OZK_MAX_SIDE || n_lo > OZK_MAX_SIDE)
+    return set_error(OZK_ERR_ARG, "n_hi must be in [1,%d] and n_lo in [0,%d]", OZK_MAX_SIDE,
+                     OZK_MAX_SIDE);
+  int n = n_hi * n_hi + 2 * n_hi * n_lo;
+  if (n > cap) return set_error(OZK_ERR_ARG, "pair capacity too small");
+  int k = 0;
+  for (int i = 0; i < n_hi; ++i)
+    for (int j = 0; j < n_hi; ++j) pa[k] = i, pb[k++] = j;
+  for (int i = 0; i < n_hi; ++i)
+    for (int j = 0; j < n_lo; ++j) pa[k] = i, pb[k++] = n_hi + j;
+  for (int i = 0; i < n_lo; ++i)
+    for (int j = 0; j < n_hi; ++j) pa[k] = n_hi + i, pb[k++] = j;
+  return n;
+}
+
+struct Workspace {
+  uint16_t* SA;
+  uint16_t* SB;
+  int32_t* eA;
+  int32_t* eB;
+  float* products;
+  size_t bytes;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Layout: SA [nS][N][k_pad] | SB [nS][M][k_pad] | eA [nS][N] | eB [nS][M] |
+// products [n_pairs][N][M] (only when materialised).
+static Workspace layout(void* base, int64_t N, int64_t K, int64_t M, int nS, int n_prod) {
+  const int64_t k_pad = round_up(K < 1 ? 1 : K, OZK_KB);
+  Workspace w;
+  size_t off = 0;
+  char* b = (char*)base;
+  w.SA = (uint16_t*)(b + off);
+  off += align256((size_t)nS * N * k_pad * 2);
+  w.SB = (uint16_t*)(b + off);
+  off += align256((size_t)nS * M * k_pad * 2);
+  w.eA = (int32_t*)(b + off);
+  off += align256((size_t)nS * N * 4);
+  w.eB = (int32_t*)(b + off);
+  off += align256((size_t)nS * M * 4);
+  w.products = (float*)(b + off);
+  off += align256((size_t)n_prod * N * M * 4);
+  w.bytes = off;
+  return w;
+}
+
+// Scoped workspace: the caller's buffer, or one from the stream-ordered pool.
+struct ScopedWs {
+  void* ptr = nullptr;
+  bool owned = false;
+  cudaStream_t s = nullptr;
+  int acquire(void* given, size_t given_bytes, size_t need, cudaStream_t stream) {
+    s = stream;
+    if (given) {
+      if (given_bytes < need)
+        return set_error(OZK_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", given_bytes, need);
+      if ((uintptr_t)given & 255) return set_error(OZK_ERR_ARG, "workspace not 256-byte aligned");
+      ptr = given;
+      return OZK_OK;
+    }
+    cudaError_t e = cudaMallocAsync(&ptr, need, stream);
+    if (e != cudaSuccess) return set_cuda_error("cudaMallocAsync(workspace)", e);
+    owned = true;
+    return OZK_OK;
+  }
+  ~ScopedWs() {
+    if (owned && ptr) cudaFreeAsync(ptr, s);
+  }
+};
+
+}  // namespace ozk
+
+using namespace ozk;
+
+extern "C" {
+
+int ozk_compute_rho_f32(int64_t K) { return rho_f32(K); }
+int ozk_compute_rho_f64(int64_t K) { return rho_f64(K); }
+
+int ozk_pair_schedule(int n_hi, int n_lo, uint8_t* pair_a, uint8_t* pair_b, int cap) {
+  if (!pair_a || !pair_b) return set_error(OZK_ERR_ARG, "NULL pair arrays");
+  return ondevice_pairs(n_hi, n_lo, pair_a, pair_b, cap);
+}
+
+int ozk_triangular_schedule(int n_slices, uint8_t* pair_a, uint8_t* pair_b, int cap) {
+  if (!pair_a || !pair_b || n_slices < 1 || n_slices > OZK_MAX_SLICES)
+    return set_error(OZK_ERR_ARG, "n_slices out of range");
+  int k = 0;
+  for (int i = 0; i < n_slices; ++i)
+    for (int j = 0; j < n_slices; ++j)
+      if (i + j <= n_slices - 1) {
+        if (k >= cap) return set_error(OZK_ERR_ARG, "pair capacity too small");
+        pair_a[k] = (uint8_t)i;
+        pair_b[k++] = (uint8_t)j;
+      }
+  return k;
+}
+
+static int check_extract_args(const void* X, int64_t ldx, int64_t lines, int64_t K, int64_t ld_min,
+                              int n_hi, int n_lo, const void* slices, int64_t k_pad,
+                              const void* exps) {
+  if (!X || !slices || !exps) return set_error(OZK_ERR_ARG, "NULL pointer");
+  if (lines < 0 || K < 1) return set_error(OZK_ERR_ARG, "bad shape");
+  if (ldx < ld_min) return set_error(OZK_ERR_ARG, "leading dimension too small");
+  if (n_hi < 1 || n_hi > OZK_MAX_SIDE || n_lo < 0 || n_lo > OZK_MAX_SIDE)
+    return set_error(OZK_ERR_ARG, "slice counts out of range");
+  if (k_pad < K || k_pad % OZK_KB) return set_error(OZK_ERR_ARG, "k_pad must be >= K and a multiple of 64");
+  if (((uintptr_t)slices & 3) != 0) return set_error(OZK_ERR_ARG, "slices not 4-byte aligned");
+  return OZK_OK;
+}
+
+int ozk_extract_rows_f64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
+                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                         int32_t* status_dev, void* stream) {
+  int rc = check_extract_args(X, ldx, rows, K, K, n_hi, n_lo, slices, k_pad, exps);
+  if (rc) return rc;
+  if (rho < 0) rho = rho_f32(K);
+  return launch_extract_rows(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status_dev,
+                             (cudaStream_t)stream);
+}
+
+int ozk_extract_cols_f64(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho, int n_hi,
+                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                         int32_t* status_dev, void* stream) {
+  int rc = check_extract_args(X, ldx, cols, K, cols, n_hi, n_lo, slices, k_pad, exps);
+  if (rc) return rc;
+  if (rho < 0) rho = rho_f32(K);
+  return launch_extract_cols(X, ldx, K, cols, rho, n_hi, n_lo, slices, k_pad, exps, status_dev,
+                             (cudaStream_t)stream);
+}
+
+int ozk_extract_rows_host_f64(const double*, int64_t, int64_t, int64_t, int, int, uint16_t*,
+                              int64_t, int32_t*, int32_t*, void*) {
+  return set_error(OZK_ERR_UNSUPPORTED, "FP64 host-pipeline extraction is not built yet");
+}
+
+int ozk_extract_cols_host_f64(const double*, int64_t, int64_t, int64_t, int, int, uint16_t*,
+                              int64_t, int32_t*, int32_t*, void*) {
+  return set_error(OZK_ERR_UNSUPPORTED, "FP64 host-pipeline extraction is not built yet");
+}
+
+int ozk_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t* SB,
+                   const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
+                   const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
+                   int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
+                   double* C, int64_t ldc, float* products, int32_t* status_dev, void* stream) {
+  if (!SA || !SB || !eA || !eB || !pair_a || !pair_b) return set_error(OZK_ERR_ARG, "NULL pointer");
+  if (N < 0 || M < 0) return set_error(OZK_ERR_ARG, "bad shape");
+  if (mode == OZK_ACC_F64 && ldc < M) return set_error(OZK_ERR_ARG, "ldc < M");
+  if (beta != 0.0 && ldcin < M) return set_error(OZK_ERR_ARG, "ldcin < M");
+  if (alpha != 1.0 && alpha != -1.0) return set_error(OZK_ERR_ARG, "alpha must be +1 or -1");
+  return launch_slice_gemm(SA, eA, nA, SB, eB, nB, N, M, k_pad, pair_a, pair_b, n_pairs, mode,
+                           symmetric, alpha, beta, Cin, ldcin, C, ldc, products, status_dev,
+                           (cudaStream_t)stream);
+}
+
+int ozk_accumulate_2sum(const float* products, const int32_t* eA, const int32_t* eB, int64_t N,
+                        int64_t M, int n_hi, int n_lo, float* C_hi, float* C_lo, double* C,
+                        int64_t ldc, void* stream) {
+  if (!products || !eA || !eB) return set_error(OZK_ERR_ARG, "NULL pointer");
+  if (N < 0 || M < 0 || n_hi < 1 || n_lo < 0) return set_error(OZK_ERR_ARG, "bad arguments");
+  if (C && ldc < M) return set_error(OZK_ERR_ARG, "ldc < M");
+  return launch_accumulate_2sum(products, eA, eB, N, M, n_hi, n_lo, C_hi, C_lo, C, ldc,
+                                (cudaStream_t)stream);
+}
+
+size_t ozk_matmul_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo) {
+  return layout(nullptr, N, K, M, n_hi + n_lo, 0).bytes;
+}
+
+static size_t matmul_ws_bytes_mode(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo, int mode) {
+  int n_prod = mode == OZK_ACC_PRODUCTS ? n_hi * n_hi + 2 * n_hi * n_lo : 0;
+  return layout(nullptr, N, K, M, n_hi + n_lo, n_prod).bytes;
+}
+
+int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
+                   int64_t ldc, int64_t N, int64_t K, int64_t M, int rho, int n_hi, int n_lo,
+                   int acc_mode, void* workspace, size_t ws_bytes, int32_t* status_dev,
+                   void* stream) {
+  if (!A || !B || !C) return set_error(OZK_ERR_ARG, "NULL pointer");
+  if (N < 0 || M < 0 || K < 1) return set_error(OZK_ERR_ARG, "bad shape (K must be >= 1)");
+  if (lda < K || ldb < M || ldc < M) return set_error(OZK_ERR_ARG, "leading dimension too small");
+  if (acc_mode != OZK_ACC_F64 && acc_mode != OZK_ACC_PRODUCTS)
+    return set_error(OZK_ERR_ARG, "bad acc_mode");
+  uint8_t pa[OZK_MAX_PAIRS], pb[OZK_MAX_PAIRS];
+  int np = ondevice_pairs(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS);
+  if (np < 0) return np;
+  if (rho < 0) rho = rho_f32(K);
+  int rc = check_bound(K, 24 - rho);
+  if (rc) return rc;
+  if (N == 0 || M == 0) return OZK_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int nS = n_hi + n_lo;
+  const int64_t k_pad = round_up(K, OZK_KB);
+  size_t need = matmul_ws_bytes_mode(N, K, M, n_hi, n_lo, acc_mode);
+  ScopedWs ws;
+  if ((rc = ws.acquire(workspace, ws_bytes, need, s))) return rc;
+  Workspace w = layout(ws.ptr, N, K, M, nS, acc_mode == OZK_ACC_PRODUCTS ? np : 0);
+  if ((rc = launch_extract_rows(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
+    return rc;
+  if ((rc = launch_extract_cols(B, ldb, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, s)))
+    return rc;
+  if (acc_mode == OZK_ACC_F64)
+    return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np, OZK_ACC_F64,
+                             0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, status_dev, s);
+  if ((rc = launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np,
+                              OZK_ACC_PRODUCTS, 0, 1.0, 0.0, nullptr, 0, nullptr, 0, w.products,
+                              status_dev, s)))
+    return rc;
+  return launch_accumulate_2sum(w.products, w.eA, w.eB, N, M, n_hi, n_lo, nullptr, nullptr, C, ldc,
+                                s);
+}
+
+size_t ozk_matmul_host_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_slices) {
+  return layout(nullptr, N, K, M, n_slices, 0).bytes;
+}
+
+int ozk_matmul_host_f64(const double*, int64_t, const double*, int64_t, double*, int64_t, int64_t,
+                        int64_t, int64_t, int, int, void*, size_t, int32_t*, void*) {
+  return set_error(OZK_ERR_UNSUPPORTED, "the FP64 host pipeline is not built yet");
+}
+
+// gram: the column extraction of A (N x K) gives, per column of A, slices over
+// the N rows -- both the row extraction of A^T and the column extraction of
+// A in the reference (gram.py:22-35), which coincide.
+size_t ozk_gram_workspace_bytes(int64_t N, int64_t K, int n_hi, int n_lo) {
+  return layout(nullptr, K, N, 0, n_hi + n_lo, 0).bytes;
+}
+
+int ozk_gram_f64(const double* A, int64_t lda, double* G, int64_t ldg, int64_t N, int64_t K,
+                 int rho, int n_hi, int n_lo, void* workspace, size_t ws_bytes,
+                 int32_t* status_dev, void* stream) {
+  if (!A || !G) return set_error(OZK_ERR_ARG, "NULL pointer");
+  if (N < 1 || K < 0) return set_error(OZK_ERR_ARG, "bad shape (N must be >= 1)");
+  if (lda < K || ldg < K) return set_error(OZK_ERR_ARG, "leading dimension too small");
+  uint8_t pa[OZK_MAX_PAIRS], pb[OZK_MAX_PAIRS];
+  int np = ondevice_pairs(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS);
+  if (np < 0) return np;
+  if (rho < 0) rho = rho_f32(N);
+  int rc = check_bound(N, 24 - rho);
+  if (rc) return rc;
+  if (K == 0) return OZK_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int nS = n_hi + n_lo;
+  const int64_t k_pad = round_up(N, OZK_KB);
+  ScopedWs ws;
+  if ((rc = ws.acquire(workspace, ws_bytes, ozk_gram_workspace_bytes(N, K, n_hi, n_lo), s)))
+    return rc;
+  Workspace w = layout(ws.ptr, K, N, 0, nS, 0);
+  if ((rc = launch_extract_cols(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
+    return rc;
+  return launch_slice_gemm(w.SA, w.eA, nS, w.SA, w.eA, nS, K, K, k_pad, pa, pb, np, OZK_ACC_F64, 1,
+                           1.0, 0.0, nullptr, 0, G, ldg, nullptr, status_dev, s);
+}
+
+size_t ozk_residual_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo) {
+  return layout(nullptr, N, K, M, n_hi + n_lo, 0).bytes;
+}
+
+int ozk_residual_f64(const double* A, int64_t lda, const double* X, int64_t ldx, const double* Bv,
+                     int64_t ldb, double* R, int64_t ldr, int64_t N, int64_t K, int64_t M, int rho,
+                     int n_hi, int n_lo, void* workspace, size_t ws_bytes, int32_t* status_dev,
+                     void* stream) {
+  if (!A || !X || !Bv || !R) return set_error(OZK_ERR_ARG, "NULL pointer");
+  if (N < 0 || M < 0 || K < 1) return set_error(OZK_ERR_ARG, "bad shape (K must be >= 1)");
+  if (lda < K || ldx < M || ldb < M || ldr < M)
+    return set_error(OZK_ERR_ARG, "leading dimension too small");
+  uint8_t pa[OZK_MAX_PAIRS], pb[OZK_MAX_PAIRS];
+  int np = ondevice_pairs(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS);
+  if (np < 0) return np;
+  if (rho < 0) rho = rho_f32(K);
+  int rc = check_bound(K, 24 - rho);
+  if (rc) return rc;
+  if (N == 0 || M == 0) return OZK_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int nS = n_hi + n_lo;
+  const int64_t k_pad = round_up(K, OZK_KB);
+  ScopedWs ws;
+  if ((rc = ws.acquire(workspace, ws_bytes, ozk_residual_workspace_bytes(N, K, M, n_hi, n_lo), s)))
+    return rc;
+  Workspace w = layout(ws.ptr, N, K, M, nS, 0);
+  if ((rc = launch_extract_rows(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
+    return rc;
+  if ((rc = launch_extract_cols(X, ldx, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, s)))
+    return rc;
+  return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np, OZK_ACC_F64, 0,
+                           -1.0, 1.0, Bv, ldb, R, ldr, nullptr, status_dev, s);
+}
+
+int ozk_check_status(const int32_t* status_dev, void* stream) {
+  if (!status_dev) return OZK_OK;
+  int32_t v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, status_dev, sizeof(v), cudaMemcpyDeviceToHost,
+                                  (cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return set_cuda_error("reading status", e);
+  if (v & OZK_FLAG_TIMEOUT) return set_error(OZK_ERR_TIMEOUT, "a device wait exceeded its budget");
+  if (v & (OZK_FLAG_NONFINITE | OZK_FLAG_RANGE))
+    return set_error(OZK_ERR_NONFINITE, "inputs contain NaN or Inf or exceed the FP32 range");
+  return OZK_OK;
+}
+
+const char* ozk_strerror(int status) {
+  switch (status) {
+    case OZK_OK: return "ok";
+    case OZK_ERR_ARG: return "invalid argument";
+    case OZK_ERR_UNSAFE: return "input violates the Ozaki exactness preflight";
+    case OZK_ERR_NONFINITE: return "input contains NaN/Inf or exceeds the FP32 range";
+    case OZK_ERR_CUDA: return "CUDA error";
+    case OZK_ERR_NCCL: return "NCCL error";
+    case OZK_ERR_TIMEOUT: return "device wait timed out";
+    case OZK_ERR_WORKSPACE: return "workspace too small";
+    case OZK_ERR_UNSUPPORTED: return "unsupported request";
+    default: return "unknown status";
+  }
+}
+
+int ozk_last_error_detail(char* buf, size_t len) {
+  if (!buf || !len) return OZK_ERR_ARG;
+  snprintf(buf, len, "%s", t_detail);
+  return OZK_OK;
+}
+
+const char* ozk_version(void) { return "ozaki-b200 0.1.0 (sm_100a)"; }
+
+}  // extern "C"

@@ -1,0 +1,347 @@
+// K1: FP64 -> double-FP32 split -> sigma-trick BF16 slices, per row (left
+// operand) or per column (right operand, written transposed so both GEMM
+// operands are K-major).  Bit-identical to the reference's
+// f32_extract_split_rows / _cols applied to _double_f32_split
+// (ozaki_jax/extract.py:116-191, ozaki_jax/matmul.py:197-213).
+//
+// Per slice t of a line (row or column) the recurrence is
+//   m = max |r|;  c = floor(RN32 log2 m) (0 if m == 0);
+//   sigma = RN32(0.75 * 2^(rho + c));  v = RN32(RN32(r + sigma) - sigma) (0 if m == 0);
+//   r = RN32(r - v);  slice = RN32(v * 2^-c)  (exactly a BF16 value).
+// Every FP32 step uses an explicit _rn intrinsic, so nothing is contracted.
+//
+// The maximum of slice t depends on slice t-1 over the whole line, so a line
+// is swept max(n_hi, n_lo) + 1 times: pass t recomputes the residual from the
+// FP64 input (an L2 hit after the first, DRAM-bound pass) and reduces its
+// maximum; the last pass emits every slice.  The FP64 input is read from DRAM
+// once when a block's lines stay resident in L2, which the launch shapes
+// below are sized for.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ozk_device.cuh"
+#include "ozk_internal.h"
+#include "ozk_log2_table.h"
+
+namespace ozk {
+
+__constant__ uint32_t c_log2_thr[OZK_LOG2_TABLE_LEN];
+
+struct SliceState {
+  float sig[OZK_MAX_SIDE];
+  float inv[OZK_MAX_SIDE];
+  int zero[OZK_MAX_SIDE];
+};
+
+// Residual of the hi (or lo) part after the first `t` slices.
+__device__ __forceinline__ float residual_after(float r, int t, const SliceState& s) {
+  for (int i = 0; i < t; ++i) {
+    float v = s.zero[i] ? 0.0f : __fsub_rn(__fadd_rn(r, s.sig[i]), s.sig[i]);
+    r = __fsub_rn(r, v);
+  }
+  return r;
+}
+
+__device__ __forceinline__ void split_f64(double x, float& hi, float& lo) {
+  hi = __double2float_rn(x);
+  lo = __double2float_rn(__dsub_rn(x, (double)hi));
+}
+
+__device__ __forceinline__ int32_t check_value(double x, float hi) {
+  int32_t f = 0;
+  if (!isfinite(x)) f |= OZK_FLAG_NONFINITE;
+  else if (!isfinite(hi)) f |= OZK_FLAG_RANGE;
+  return f;
+}
+
+// Slice parameters from a line maximum (extract.py:125-137).
+__device__ __forceinline__ void slice_params(float m, int rho, float& sig, float& inv, int& zero,
+                                             int& c) {
+  zero = (m == 0.0f);
+  c = zero ? 0 : floor_log2_rn32(m, c_log2_thr);
+  sig = __fmul_rn(0.75f, pow2f(rho + c));
+  inv = pow2f(-c);
+}
+
+// ---------------------------------------------------------------- rows
+
+template <int NT>
+__global__ void __launch_bounds__(NT) k_extract_rows(const double* __restrict__ X, int64_t ldx,
+                                                     int64_t rows, int64_t K, int rho, int n_hi,
+                                                     int n_lo, uint16_t* __restrict__ slices,
+                                                     int64_t k_pad, int32_t* __restrict__ exps,
+                                                     int32_t* status) {
+  __shared__ SliceState s_hi, s_lo;
+  __shared__ float s_red[2][NT / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int npass = n_hi > n_lo ? n_hi : n_lo;
+  const int64_t slice_stride = rows * k_pad;
+
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const double* x = X + row * ldx;
+    int32_t flags = 0;
+    for (int t = 0; t < npass; ++t) {
+      float mh = 0.0f, ml = 0.0f;
+      for (int64_t k = tid; k < K; k += NT) {
+        double xv = __ldg(x + k);
+        float hi, lo;
+        split_f64(xv, hi, lo);
+        if (t == 0) flags |= check_value(xv, hi);
+        if (t < n_hi) mh = fmaxf(mh, fabsf(residual_after(hi, t, s_hi)));
+        if (t < n_lo) ml = fmaxf(ml, fabsf(residual_after(lo, t, s_lo)));
+      }
+      for (int o = 16; o; o >>= 1) {
+        mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
+        ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, o));
+      }
+      if (lane == 0) {
+        s_red[0][warp] = mh;
+        s_red[1][warp] = ml;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        for (int w = 1; w < NT / 32; ++w) {
+          mh = fmaxf(mh, s_red[0][w]);
+          ml = fmaxf(ml, s_red[1][w]);
+        }
+        int c;
+        if (t < n_hi) {
+          slice_params(mh, rho, s_hi.sig[t], s_hi.inv[t], s_hi.zero[t], c);
+          exps[(int64_t)t * rows + row] = c;
+        }
+        if (t < n_lo) {
+          slice_params(ml, rho, s_lo.sig[t], s_lo.inv[t], s_lo.zero[t], c);
+          exps[(int64_t)(n_hi + t) * rows + row] = c;
+        }
+      }
+      __syncthreads();
+    }
+    if (flags) raise_flag(status, flags);
+    // Emit pass: two columns per thread per step, written as one 32-bit word.
+    uint16_t* out = slices + row * k_pad;
+    for (int64_t k = 2 * tid; k < k_pad; k += 2 * NT) {
+      uint32_t wh[OZK_MAX_SIDE], wl[OZK_MAX_SIDE];
+#pragma unroll
+      for (int i = 0; i < OZK_MAX_SIDE; ++i) wh[i] = wl[i] = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (k + h < K) {
+          float rh, rl;
+          split_f64(__ldg(x + k + h), rh, rl);
+#pragma unroll
+          for (int i = 0; i < OZK_MAX_SIDE; ++i) {
+            if (i < n_hi) {
+              float v = s_hi.zero[i] ? 0.0f : __fsub_rn(__fadd_rn(rh, s_hi.sig[i]), s_hi.sig[i]);
+              rh = __fsub_rn(rh, v);
+              wh[i] |= (uint32_t)bf16_bits_exact(__fmul_rn(v, s_hi.inv[i])) << (16 * h);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < OZK_MAX_SIDE; ++i) {
+            if (i < n_lo) {
+              float v = s_lo.zero[i] ? 0.0f : __fsub_rn(__fadd_rn(rl, s_lo.sig[i]), s_lo.sig[i]);
+              rl = __fsub_rn(rl, v);
+              wl[i] |= (uint32_t)bf16_bits_exact(__fmul_rn(v, s_lo.inv[i])) << (16 * h);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < OZK_MAX_SIDE; ++i)
+        if (i < n_hi) *reinterpret_cast<uint32_t*>(out + i * slice_stride + k) = wh[i];
+#pragma unroll
+      for (int i = 0; i < OZK_MAX_SIDE; ++i)
+        if (i < n_lo) *reinterpret_cast<uint32_t*>(out + (n_hi + i) * slice_stride + k) = wl[i];
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------- columns
+
+// A block owns 32 adjacent columns (lane = column) and all K rows; its 8
+// warps split the rows.  The emit pass stages 64 rows x 32 columns per slice
+// in shared memory and writes them transposed, 128 bytes per column.
+constexpr int kColW = 32;
+constexpr int kColNT = 256;
+constexpr int kColChunk = 64;
+
+__global__ void __launch_bounds__(kColNT) k_extract_cols(const double* __restrict__ X, int64_t ldx,
+                                                         int64_t K, int64_t cols, int rho,
+                                                         int n_hi, int n_lo,
+                                                         uint16_t* __restrict__ slices,
+                                                         int64_t k_pad, int32_t* __restrict__ exps,
+                                                         int32_t* status) {
+  __shared__ float s_sig[2][OZK_MAX_SIDE][kColW];
+  __shared__ float s_inv[2][OZK_MAX_SIDE][kColW];
+  __shared__ int s_zero[2][OZK_MAX_SIDE][kColW];
+  __shared__ float s_red[2][kColNT / 32][kColW];
+  // [slice][column][k] staging for the transposed write (+2 to spread banks).
+  extern __shared__ uint16_t s_tile[];
+  constexpr int kRowPitch = kColChunk + 2;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int npass = n_hi > n_lo ? n_hi : n_lo;
+  const int ns = n_hi + n_lo;
+  const int64_t slice_stride = cols * k_pad;
+
+  for (int64_t c0 = (int64_t)blockIdx.x * kColW; c0 < cols; c0 += (int64_t)gridDim.x * kColW) {
+    const int64_t col = c0 + lane;
+    const bool valid = col < cols;
+    int32_t flags = 0;
+    for (int t = 0; t < npass; ++t) {
+      float mh = 0.0f, ml = 0.0f;
+      if (valid) {
+        for (int64_t k = warp; k < K; k += kColNT / 32) {
+          double xv = __ldg(X + k * ldx + col);
+          float hi, lo;
+          split_f64(xv, hi, lo);
+          if (t == 0) flags |= check_value(xv, hi);
+          float rh = hi, rl = lo;
+          for (int i = 0; i < t; ++i) {
+            if (i < n_hi) {
+              float sg = s_sig[0][i][lane];
+              float v = s_zero[0][i][lane] ? 0.0f : __fsub_rn(__fadd_rn(rh, sg), sg);
+              rh = __fsub_rn(rh, v);
+            }
+            if (i < n_lo) {
+              float sg = s_sig[1][i][lane];
+              float v = s_zero[1][i][lane] ? 0.0f : __fsub_rn(__fadd_rn(rl, sg), sg);
+              rl = __fsub_rn(rl, v);
+            }
+          }
+          if (t < n_hi) mh = fmaxf(mh, fabsf(rh));
+          if (t < n_lo) ml = fmaxf(ml, fabsf(rl));
+        }
+      }
+      s_red[0][warp][lane] = mh;
+      s_red[1][warp][lane] = ml;
+      __syncthreads();
+      if (warp == 0) {
+        for (int w = 1; w < kColNT / 32; ++w) {
+          mh = fmaxf(mh, s_red[0][w][lane]);
+          ml = fmaxf(ml, s_red[1][w][lane]);
+        }
+        int c;
+        if (t < n_hi) {
+          slice_params(mh, rho, s_sig[0][t][lane], s_inv[0][t][lane], s_zero[0][t][lane], c);
+          if (valid) exps[(int64_t)t * cols + col] = c;
+        }
+        if (t < n_lo) {
+          slice_params(ml, rho, s_sig[1][t][lane], s_inv[1][t][lane], s_zero[1][t][lane], c);
+          if (valid) exps[(int64_t)(n_hi + t) * cols + col] = c;
+        }
+      }
+      __syncthreads();
+    }
+    if (flags) raise_flag(status, flags);
+
+    for (int64_t k0 = 0; k0 < k_pad; k0 += kColChunk) {
+      // compute: each thread handles rows k0 + warp + 8*j of its column
+      for (int j = 0; j < kColChunk / (kColNT / 32); ++j) {
+        int kk = warp + j * (kColNT / 32);
+        int64_t k = k0 + kk;
+        float rh = 0.0f, rl = 0.0f;
+        bool live = valid && k < K;
+        if (live) split_f64(__ldg(X + k * ldx + col), rh, rl);
+        for (int i = 0; i < n_hi; ++i) {
+          float v = 0.0f;
+          if (live) {
+            float sg = s_sig[0][i][lane];
+            v = s_zero[0][i][lane] ? 0.0f : __fsub_rn(__fadd_rn(rh, sg), sg);
+            rh = __fsub_rn(rh, v);
+            v = __fmul_rn(v, s_inv[0][i][lane]);
+          }
+          s_tile[(i * kColW + lane) * kRowPitch + kk] = bf16_bits_exact(v);
+        }
+        for (int i = 0; i < n_lo; ++i) {
+          float v = 0.0f;
+          if (live) {
+            float sg = s_sig[1][i][lane];
+            v = s_zero[1][i][lane] ? 0.0f : __fsub_rn(__fadd_rn(rl, sg), sg);
+            rl = __fsub_rn(rl, v);
+            v = __fmul_rn(v, s_inv[1][i][lane]);
+          }
+          s_tile[((n_hi + i) * kColW + lane) * kRowPitch + kk] = bf16_bits_exact(v);
+        }
+      }
+      __syncthreads();
+      // write: per slice, 32 columns x 64 k; a thread writes 4 consecutive k.
+      for (int e = tid; e < ns * kColW * (kColChunk / 4); e += kColNT) {
+        int q = e % (kColChunk / 4);
+        int cl = (e / (kColChunk / 4)) % kColW;
+        int s = e / ((kColChunk / 4) * kColW);
+        int64_t cc = c0 + cl;
+        if (cc < cols) {
+          const uint16_t* src = &s_tile[(s * kColW + cl) * kRowPitch + 4 * q];
+          uint2 w;
+          w.x = (uint32_t)src[0] | ((uint32_t)src[1] << 16);
+          w.y = (uint32_t)src[2] | ((uint32_t)src[3] << 16);
+          *reinterpret_cast<uint2*>(slices + s * slice_stride + cc * k_pad + k0 + 4 * q) = w;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+static int g_table_uploaded[64] = {0};
+
+int upload_log2_table(int dev) {
+  if (dev < 0 || dev >= 64) return OZK_ERR_ARG;
+  if (g_table_uploaded[dev]) return OZK_OK;
+  cudaError_t e = cudaMemcpyToSymbol(c_log2_thr, kOzkLog2ThreshHost, sizeof(kOzkLog2ThreshHost));
+  if (e != cudaSuccess) return set_cuda_error("cudaMemcpyToSymbol(log2 table)", e);
+  g_table_uploaded[dev] = 1;
+  return OZK_OK;
+}
+
+int launch_extract_rows(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
+                        int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
+                        cudaStream_t stream) {
+  if (rows == 0) return OZK_OK;
+  int dev;
+  cudaGetDevice(&dev);
+  int rc = upload_log2_table(dev);
+  if (rc) return rc;
+  // Keep the lines in flight within a few tens of MB so passes 2.. hit L2.
+  int sms = device_sm_count(dev);
+  int64_t per_sm = K <= 4096 ? 8 : (K <= 16384 ? 4 : 2);
+  int64_t grid = rows < sms * per_sm ? rows : sms * per_sm;
+  if (K > 8192) {
+    k_extract_rows<512><<<(unsigned)grid, 512, 0, stream>>>(X, ldx, rows, K, rho, n_hi, n_lo,
+                                                             slices, k_pad, exps, status);
+  } else {
+    k_extract_rows<256><<<(unsigned)grid, 256, 0, stream>>>(X, ldx, rows, K, rho, n_hi, n_lo,
+                                                             slices, k_pad, exps, status);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows launch", e);
+}
+
+int launch_extract_cols(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho, int n_hi,
+                        int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
+                        cudaStream_t stream) {
+  if (cols == 0) return OZK_OK;
+  int dev;
+  cudaGetDevice(&dev);
+  int rc = upload_log2_table(dev);
+  if (rc) return rc;
+  size_t smem = (size_t)(n_hi + n_lo) * kColW * (kColChunk + 2) * sizeof(uint16_t);
+  static int configured[64] = {0};
+  if (!configured[dev]) {
+    cudaFuncSetAttribute(k_extract_cols, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    configured[dev] = 1;
+  }
+  int64_t strips = (cols + kColW - 1) / kColW;
+  int sms = device_sm_count(dev);
+  int64_t grid = strips < 2 * sms ? strips : 2 * sms;
+  k_extract_cols<<<(unsigned)grid, kColNT, smem, stream>>>(X, ldx, K, cols, rho, n_hi, n_lo,
+                                                            slices, k_pad, exps, status);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_cols launch", e);
+}
+
+}  // namespace ozk

@@ -1,0 +1,104 @@
+"""CPU-only checks of the boundary: the C-ABI library loads, exports every
+symbol the header declares, and its host-side policies match the reference."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "ozaki_b200.h")
+
+
+def header_functions():
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(ozk_\w+)\s*\(", txt)))
+
+
+def test_library_exports_every_declared_symbol():
+    from ozaki_jax_b200 import _lib
+    lib = _lib.load()
+    names = header_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    # every binding in the Python layer is declared in the header
+    assert set(_lib.SIGNATURES) <= set(names)
+
+
+def test_version_and_strerror():
+    from ozaki_jax_b200 import _lib
+    lib = _lib.load()
+    assert b"sm_100a" in lib.ozk_version()
+    for code in range(-8, 1):
+        assert lib.ozk_strerror(code)
+
+
+def test_rho_policy_matches_reference(golden):
+    from ozaki_jax_b200 import _lib
+    _, meta = golden
+    lib = _lib.load()
+    for K, rho in meta["rho_f32"].items():
+        assert lib.ozk_compute_rho_f32(int(K)) == rho, K
+    for K, rho in meta["rho_f64"].items():
+        assert lib.ozk_compute_rho_f64(int(K)) == rho, K
+
+
+def test_pair_schedule_matches_reference(golden):
+    from ozaki_jax_b200 import _lib
+    _, meta = golden
+    lib = _lib.load()
+    for key, ref in meta["pair_schedule"].items():
+        n_hi, n_lo = map(int, key.split(","))
+        pa = (ctypes.c_uint8 * 256)()
+        pb = (ctypes.c_uint8 * 256)()
+        n = lib.ozk_pair_schedule(n_hi, n_lo, pa, pb, 256)
+        assert n == ref["n_pairs"]
+        assert list(pa[:n]) == ref["pair_a"] and list(pb[:n]) == ref["pair_b"]
+    pa = (ctypes.c_uint8 * 256)()
+    pb = (ctypes.c_uint8 * 256)()
+    n = lib.ozk_triangular_schedule(8, pa, pb, 256)
+    assert n == 36
+    assert [(a, b) for a, b in zip(pa[:n], pb[:n])] == \
+        [(i, j) for i in range(8) for j in range(8) if i + j <= 7]
+
+
+def test_argument_errors_return_codes():
+    from ozaki_jax_b200 import _lib
+    lib = _lib.load()
+    # NULL pointers and bad shapes are refused before any device work
+    assert lib.ozk_matmul_f64(None, 1, None, 1, None, 1, 1, 1, 1, -1, 4, 1, 0, None, 0, None,
+                              None) == _lib.OZK_ERR_ARG
+    assert lib.ozk_pair_schedule(0, 1, None, None, 0) == _lib.OZK_ERR_ARG
+    assert lib.ozk_slice_gemm(None, None, 1, None, None, 1, 1, 1, 64, None, None, 1, 0, 0, 1.0,
+                              0.0, None, 0, None, 0, None, None, None) == _lib.OZK_ERR_ARG
+    assert "NULL" in _lib.detail()
+
+
+def test_log2_table_matches_numpy_log2():
+    """The device's exponent rule floor(RN32(log2 m)) (a per-binade threshold
+    table) agrees with NumPy's float32 log2 -- the reference's rule,
+    ozaki_jax/extract.py:130 -- around every binade edge and at random."""
+    txt = open(os.path.join(ROOT, "ozaki_jax_b200", "csrc", "ozk_log2_table.h")).read()
+    tab = np.array([int(x, 16) for x in re.findall(r"0x([0-9a-f]{8})u", txt)], dtype=np.int64)
+    assert len(tab) == 277
+
+    def rule(m):
+        b = m.view(np.uint32).astype(np.int64)
+        sub = -149 + np.floor(np.log2(np.maximum(b, 1).astype(np.float64))).astype(np.int64)
+        e = np.where(b >= 0x00800000, (b >> 23) - 127, sub)
+        return e + (b >= tab[e + 149])
+
+    ids = []
+    for e in range(-149, 128):
+        base = int(np.float32(2.0 ** e).view(np.uint32))
+        ids.append(np.arange(base - 200, base + 200, dtype=np.int64))
+    ids = np.concatenate(ids + [np.random.default_rng(1).integers(1, 0x7F800000, 2_000_000)])
+    ids = ids[(ids > 0) & (ids < 0x7F800000)]
+    m = ids.astype(np.uint32).view(np.float32)
+    ref = np.floor(np.log2(m).astype(np.float32)).astype(np.int64)
+    assert np.array_equal(rule(m), ref)

@@ -213,14 +213,28 @@ int ozk_extract_cols_f64(const double* X, int64_t ldx, int64_t K, int64_t cols, 
                              (cudaStream_t)stream);
 }
 
-int ozk_extract_rows_host_f64(const double*, int64_t, int64_t, int64_t, int, int, uint16_t*,
-                              int64_t, int32_t*, int32_t*, void*) {
-  return set_error(OZK_ERR_UNSUPPORTED, "FP64 host-pipeline extraction is not built yet");
+int ozk_extract_rows_host_f64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                              int n_slices, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                              int32_t* status_dev, void* stream) {
+  if (n_slices < 1 || n_slices > OZK_MAX_SLICES)
+    return set_error(OZK_ERR_ARG, "n_slices must be in [1,%d]", OZK_MAX_SLICES);
+  int rc = check_extract_args(X, ldx, rows, K, K, 1, 0, slices, k_pad, exps);
+  if (rc) return rc;
+  if (rho < 0) rho = rho_f64(K);
+  return launch_extract_rows64(X, ldx, rows, K, rho, n_slices, slices, k_pad, exps, status_dev,
+                               (cudaStream_t)stream);
 }
 
-int ozk_extract_cols_host_f64(const double*, int64_t, int64_t, int64_t, int, int, uint16_t*,
-                              int64_t, int32_t*, int32_t*, void*) {
-  return set_error(OZK_ERR_UNSUPPORTED, "FP64 host-pipeline extraction is not built yet");
+int ozk_extract_cols_host_f64(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho,
+                              int n_slices, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                              int32_t* status_dev, void* stream) {
+  if (n_slices < 1 || n_slices > OZK_MAX_SLICES)
+    return set_error(OZK_ERR_ARG, "n_slices must be in [1,%d]", OZK_MAX_SLICES);
+  int rc = check_extract_args(X, ldx, cols, K, cols, 1, 0, slices, k_pad, exps);
+  if (rc) return rc;
+  if (rho < 0) rho = rho_f64(K);
+  return launch_extract_cols64(X, ldx, K, cols, rho, n_slices, slices, k_pad, exps, status_dev,
+                               (cudaStream_t)stream);
 }
 
 int ozk_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t* SB,
@@ -299,9 +313,36 @@ size_t ozk_matmul_host_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_sl
   return layout(nullptr, N, K, M, n_slices, 0).bytes;
 }
 
-int ozk_matmul_host_f64(const double*, int64_t, const double*, int64_t, double*, int64_t, int64_t,
-                        int64_t, int64_t, int, int, void*, size_t, int32_t*, void*) {
-  return set_error(OZK_ERR_UNSUPPORTED, "the FP64 host pipeline is not built yet");
+int ozk_matmul_host_f64(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
+                        int64_t ldc, int64_t N, int64_t K, int64_t M, int rho, int n_slices,
+                        void* workspace, size_t ws_bytes, int32_t* status_dev, void* stream) {
+  if (!A || !B || !C) return set_error(OZK_ERR_ARG, "NULL pointer");
+  if (N < 0 || M < 0 || K < 1) return set_error(OZK_ERR_ARG, "bad shape (K must be >= 1)");
+  if (lda < K || ldb < M || ldc < M) return set_error(OZK_ERR_ARG, "leading dimension too small");
+  if (n_slices < 1 || n_slices > OZK_MAX_SLICES)
+    return set_error(OZK_ERR_ARG, "n_slices must be in [1,%d]", OZK_MAX_SLICES);
+  uint8_t pa[OZK_MAX_PAIRS], pb[OZK_MAX_PAIRS];
+  int np = ozk_triangular_schedule(n_slices, pa, pb, OZK_MAX_PAIRS);
+  if (np < 0) return np;
+  if (rho < 0) rho = rho_f64(K);
+  int rc = check_bound(K, 53 - rho);
+  if (rc) return rc;
+  if (n_slices * (53 - rho) < 53)
+    return set_error(OZK_ERR_UNSAFE, "insufficient slice budget: n_slices*bits_per_slice=%d < 53",
+                     n_slices * (53 - rho));
+  if (N == 0 || M == 0) return OZK_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t k_pad = round_up(K, OZK_KB);
+  ScopedWs ws;
+  if ((rc = ws.acquire(workspace, ws_bytes, ozk_matmul_host_workspace_bytes(N, K, M, n_slices), s)))
+    return rc;
+  Workspace w = layout(ws.ptr, N, K, M, n_slices, 0);
+  if ((rc = launch_extract_rows64(A, lda, N, K, rho, n_slices, w.SA, k_pad, w.eA, status_dev, s)))
+    return rc;
+  if ((rc = launch_extract_cols64(B, ldb, K, M, rho, n_slices, w.SB, k_pad, w.eB, status_dev, s)))
+    return rc;
+  return launch_slice_gemm(w.SA, w.eA, n_slices, w.SB, w.eB, n_slices, N, M, k_pad, pa, pb, np,
+                           OZK_ACC_F64, 0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, status_dev, s);
 }
 
 // gram: the column extraction of A (N x K) gives, per column of A, slices over

@@ -26,6 +26,15 @@
 namespace ozk {
 
 __constant__ uint32_t c_log2_thr[OZK_LOG2_TABLE_LEN];
+__constant__ unsigned long long c_log2_thr64[OZK_LOG2_TABLE64_LEN];
+
+// floor(RN64(log2 m)) for finite m > 0 (ozaki_jax/extract.py:37, :82).
+__device__ __forceinline__ int floor_log2_rn64(double m) {
+  unsigned long long b = (unsigned long long)__double_as_longlong(m);
+  int ex = (int)(b >> 52);
+  int e = ex > 0 ? ex - 1023 : -1074 + (63 - __clzll((long long)b));
+  return e + (b >= c_log2_thr64[e + 1074] ? 1 : 0);
+}
 
 struct SliceState {
   float sig[OZK_MAX_SIDE];
@@ -285,6 +294,174 @@ __global__ void __launch_bounds__(kColNT) k_extract_cols(const double* __restric
   }
 }
 
+// ---------------------------------------------------------------- FP64 (host pipeline)
+
+// The host pipeline's extraction (extract_split_rows / _cols,
+// ozaki_jax/extract.py:21-103): the same recurrence on the FP64 input itself,
+// in FP64, n_slices slices; each normalised slice is rounded to FP32 storage
+// by the reference and is exactly a BF16 value (at most 54 - rho <= 8 bits).
+struct SliceState64 {
+  double sig[OZK_MAX_SLICES];
+  double inv[OZK_MAX_SLICES];
+  int zero[OZK_MAX_SLICES];
+};
+
+__device__ __forceinline__ void slice_params64(double m, int rho, double& sig, double& inv,
+                                               int& zero, int& c) {
+  zero = (m == 0.0);
+  c = zero ? 0 : floor_log2_rn64(m);
+  sig = __dmul_rn(0.75, pow2d(rho + c));
+  inv = pow2d(-c);
+}
+
+__device__ __forceinline__ uint16_t slice_bits64(double v, double inv) {
+  return bf16_bits_exact(__double2float_rn(__dmul_rn(v, inv)));
+}
+
+template <int NT>
+__global__ void __launch_bounds__(NT) k_extract_rows64(const double* __restrict__ X, int64_t ldx,
+                                                       int64_t rows, int64_t K, int rho, int ns,
+                                                       uint16_t* __restrict__ slices,
+                                                       int64_t k_pad, int32_t* __restrict__ exps,
+                                                       int32_t* status) {
+  __shared__ SliceState64 st;
+  __shared__ double s_red[NT / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t slice_stride = rows * k_pad;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const double* x = X + row * ldx;
+    int32_t flags = 0;
+    for (int t = 0; t < ns; ++t) {
+      double m = 0.0;
+      for (int64_t k = tid; k < K; k += NT) {
+        double r = __ldg(x + k);
+        if (t == 0 && !isfinite(r)) flags |= OZK_FLAG_NONFINITE;
+        for (int i = 0; i < t; ++i) {
+          double v = st.zero[i] ? 0.0 : __dsub_rn(__dadd_rn(r, st.sig[i]), st.sig[i]);
+          r = __dsub_rn(r, v);
+        }
+        m = fmax(m, fabs(r));
+      }
+      for (int o = 16; o; o >>= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) s_red[warp] = m;
+      __syncthreads();
+      if (tid == 0) {
+        for (int w = 1; w < NT / 32; ++w) m = fmax(m, s_red[w]);
+        int c;
+        slice_params64(m, rho, st.sig[t], st.inv[t], st.zero[t], c);
+        exps[(int64_t)t * rows + row] = c;
+      }
+      __syncthreads();
+    }
+    if (flags) raise_flag(status, flags);
+    uint16_t* out = slices + row * k_pad;
+    for (int64_t k = 2 * tid; k < k_pad; k += 2 * NT) {
+      uint32_t w[OZK_MAX_SLICES];
+#pragma unroll
+      for (int i = 0; i < OZK_MAX_SLICES; ++i) w[i] = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (k + h < K) {
+          double r = __ldg(x + k + h);
+#pragma unroll
+          for (int i = 0; i < OZK_MAX_SLICES; ++i) {
+            if (i < ns) {
+              double v = st.zero[i] ? 0.0 : __dsub_rn(__dadd_rn(r, st.sig[i]), st.sig[i]);
+              r = __dsub_rn(r, v);
+              w[i] |= (uint32_t)slice_bits64(v, st.inv[i]) << (16 * h);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < OZK_MAX_SLICES; ++i)
+        if (i < ns) *reinterpret_cast<uint32_t*>(out + i * slice_stride + k) = w[i];
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kColNT) k_extract_cols64(const double* __restrict__ X,
+                                                           int64_t ldx, int64_t K, int64_t cols,
+                                                           int rho, int ns,
+                                                           uint16_t* __restrict__ slices,
+                                                           int64_t k_pad,
+                                                           int32_t* __restrict__ exps,
+                                                           int32_t* status) {
+  __shared__ double s_sig[OZK_MAX_SLICES][kColW];
+  __shared__ double s_inv[OZK_MAX_SLICES][kColW];
+  __shared__ int s_zero[OZK_MAX_SLICES][kColW];
+  __shared__ double s_red[kColNT / 32][kColW];
+  extern __shared__ uint16_t s_tile[];
+  constexpr int kRowPitch = kColChunk + 2;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t slice_stride = cols * k_pad;
+
+  for (int64_t c0 = (int64_t)blockIdx.x * kColW; c0 < cols; c0 += (int64_t)gridDim.x * kColW) {
+    const int64_t col = c0 + lane;
+    const bool valid = col < cols;
+    int32_t flags = 0;
+    for (int t = 0; t < ns; ++t) {
+      double m = 0.0;
+      if (valid) {
+        for (int64_t k = warp; k < K; k += kColNT / 32) {
+          double r = __ldg(X + k * ldx + col);
+          if (t == 0 && !isfinite(r)) flags |= OZK_FLAG_NONFINITE;
+          for (int i = 0; i < t; ++i) {
+            double sg = s_sig[i][lane];
+            double v = s_zero[i][lane] ? 0.0 : __dsub_rn(__dadd_rn(r, sg), sg);
+            r = __dsub_rn(r, v);
+          }
+          m = fmax(m, fabs(r));
+        }
+      }
+      s_red[warp][lane] = m;
+      __syncthreads();
+      if (warp == 0) {
+        for (int w = 1; w < kColNT / 32; ++w) m = fmax(m, s_red[w][lane]);
+        int c;
+        slice_params64(m, rho, s_sig[t][lane], s_inv[t][lane], s_zero[t][lane], c);
+        if (valid) exps[(int64_t)t * cols + col] = c;
+      }
+      __syncthreads();
+    }
+    if (flags) raise_flag(status, flags);
+    for (int64_t k0 = 0; k0 < k_pad; k0 += kColChunk) {
+      for (int j = 0; j < kColChunk / (kColNT / 32); ++j) {
+        int kk = warp + j * (kColNT / 32);
+        int64_t k = k0 + kk;
+        bool live = valid && k < K;
+        double r = live ? __ldg(X + k * ldx + col) : 0.0;
+        for (int i = 0; i < ns; ++i) {
+          uint16_t bits = 0;
+          if (live) {
+            double sg = s_sig[i][lane];
+            double v = s_zero[i][lane] ? 0.0 : __dsub_rn(__dadd_rn(r, sg), sg);
+            r = __dsub_rn(r, v);
+            bits = slice_bits64(v, s_inv[i][lane]);
+          }
+          s_tile[(i * kColW + lane) * kRowPitch + kk] = bits;
+        }
+      }
+      __syncthreads();
+      for (int e = tid; e < ns * kColW * (kColChunk / 4); e += kColNT) {
+        int q = e % (kColChunk / 4);
+        int cl = (e / (kColChunk / 4)) % kColW;
+        int s = e / ((kColChunk / 4) * kColW);
+        int64_t cc = c0 + cl;
+        if (cc < cols) {
+          const uint16_t* src = &s_tile[(s * kColW + cl) * kRowPitch + 4 * q];
+          uint2 w;
+          w.x = (uint32_t)src[0] | ((uint32_t)src[1] << 16);
+          w.y = (uint32_t)src[2] | ((uint32_t)src[3] << 16);
+          *reinterpret_cast<uint2*>(slices + s * slice_stride + cc * k_pad + k0 + 4 * q) = w;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
 // ---------------------------------------------------------------- host side
 
 static int g_table_uploaded[64] = {0};
@@ -293,6 +470,8 @@ int upload_log2_table(int dev) {
   if (dev < 0 || dev >= 64) return OZK_ERR_ARG;
   if (g_table_uploaded[dev]) return OZK_OK;
   cudaError_t e = cudaMemcpyToSymbol(c_log2_thr, kOzkLog2ThreshHost, sizeof(kOzkLog2ThreshHost));
+  if (e == cudaSuccess)
+    e = cudaMemcpyToSymbol(c_log2_thr64, kOzkLog2Thresh64Host, sizeof(kOzkLog2Thresh64Host));
   if (e != cudaSuccess) return set_cuda_error("cudaMemcpyToSymbol(log2 table)", e);
   g_table_uploaded[dev] = 1;
   return OZK_OK;
@@ -342,6 +521,46 @@ int launch_extract_cols(const double* X, int64_t ldx, int64_t K, int64_t cols, i
                                                             slices, k_pad, exps, status);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_cols launch", e);
+}
+
+int launch_extract_rows64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int ns,
+                          uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
+                          cudaStream_t stream) {
+  if (rows == 0) return OZK_OK;
+  int dev;
+  cudaGetDevice(&dev);
+  int rc = upload_log2_table(dev);
+  if (rc) return rc;
+  int sms = device_sm_count(dev);
+  int64_t per_sm = K <= 4096 ? 8 : (K <= 16384 ? 4 : 2);
+  int64_t grid = rows < sms * per_sm ? rows : sms * per_sm;
+  k_extract_rows64<256><<<(unsigned)grid, 256, 0, stream>>>(X, ldx, rows, K, rho, ns, slices,
+                                                             k_pad, exps, status);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows64 launch", e);
+}
+
+int launch_extract_cols64(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho, int ns,
+                          uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
+                          cudaStream_t stream) {
+  if (cols == 0) return OZK_OK;
+  int dev;
+  cudaGetDevice(&dev);
+  int rc = upload_log2_table(dev);
+  if (rc) return rc;
+  size_t smem = (size_t)ns * kColW * (kColChunk + 2) * sizeof(uint16_t);
+  static int configured[64] = {0};
+  if (!configured[dev]) {
+    cudaFuncSetAttribute(k_extract_cols64, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    configured[dev] = 1;
+  }
+  int64_t strips = (cols + kColW - 1) / kColW;
+  int sms = device_sm_count(dev);
+  int64_t grid = strips < 2 * sms ? strips : 2 * sms;
+  k_extract_cols64<<<(unsigned)grid, kColNT, smem, stream>>>(X, ldx, K, cols, rho, ns, slices,
+                                                              k_pad, exps, status);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_cols64 launch", e);
 }
 
 }  // namespace ozk

@@ -95,11 +95,6 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& tm, i
   tn = r / gsz;
 }
 
-__device__ __forceinline__ double scale_pow2(int e) {
-  if (e >= -1022 && e <= 1023) return __longlong_as_double((long long)(e + 1023) << 52);
-  return pow2d(e);
-}
-
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     k_slice_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
@@ -286,8 +281,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               acc = __hiloint2double((int)H[j], (int)L[j]);
             }
-            const double sc = g.alpha * scale_pow2(ea + s_eB[b * BN + c0 + j]);
-            acc = fma((double)__uint_as_float(P[j]), sc, acc);
+            const int eb = s_eB[b * BN + c0 + j];
+            const double pj = (double)__uint_as_float(P[j]);
+            if (ea + eb >= -1022 && ea + eb <= 1023)
+              acc = fma(pj, g.alpha * __longlong_as_double((long long)(ea + eb + 1023) << 52), acc);
+            else  // outside the normal range: scale in two exact steps
+              acc = fma(pj * pow2d(ea), g.alpha * pow2d(eb), acc);
             if (last) {
               L[j] = (uint32_t)__double2loint(acc);
               H[j] = (uint32_t)__double2hiint(acc);

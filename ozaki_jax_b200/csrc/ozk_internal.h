@@ -28,6 +28,12 @@ int launch_extract_rows(const double* X, int64_t ldx, int64_t rows, int64_t K, i
 int launch_extract_cols(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho, int n_hi,
                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
                         cudaStream_t stream);
+int launch_extract_rows64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int ns,
+                          uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
+                          cudaStream_t stream);
+int launch_extract_cols64(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho, int ns,
+                          uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
+                          cudaStream_t stream);
 int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t* SB,
                       const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
                       const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,

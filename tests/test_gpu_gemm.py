@@ -154,9 +154,10 @@ def test_fp64_epilogue_matches_fp64_oracle(golden, name):
         # distance to the FP64-accumulating reference: rounding level of |A||B|
         scale = np.abs(A) @ np.abs(B)
         assert np.all(np.abs(C - ref) <= 64 * 2.0 ** -52 * scale + 1e-300), pname
-        # accuracy no worse than the reference's (and than its fused path)
+        # accuracy no worse than 1.5x the reference's; below 32 ulps of FP64 the
+        # Ozaki truncation is gone and only FP64 summation order remains
         e_ref = min(O.rel_err(ref, E), O.rel_err(arrays[f"{name}/{pname}/fused"], E))
-        assert O.rel_err(C, E) <= 1.5 * e_ref + 1e-16, pname
+        assert O.rel_err(C, E) <= max(1.5 * e_ref, 32 * 2.0 ** -52), pname
 
 
 def test_accuracy_gate_256x8192x256(golden):

@@ -144,6 +144,23 @@ int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, d
                    int acc_mode, void* workspace, size_t ws_bytes, int32_t* status_dev,
                    void* stream);
 
+/* Allocation-free variant of ozk_matmul_f64 (acc_mode OZK_ACC_F64, rho from K).
+ * It has no counterpart in the reference.  For callers that must not allocate
+ * device memory during a call (a process whose framework owns the GPU's memory,
+ * such as JAX/XLA reserving most of it for its own allocator, or a plugin
+ * callback its host forbids from allocating): the slice workspace comes from a
+ * fixed device array of OZK_NOALLOC_SCRATCH_BYTES compiled into the library,
+ * held by every GPU that loads it until exit.  Requests whose workspace
+ * (ozk_matmul_workspace_bytes) exceeds it return OZK_ERR_WORKSPACE;
+ * 1024 x 1024 x 1024 at (4, 1) fits.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) and should come before any
+ * stream capture.  All calls share the array; calls that overlap on the GPU
+ * race on it and must be serialised by the caller.  No cudaMalloc/cudaFree. */
+#define OZK_NOALLOC_SCRATCH_BYTES (32 * 1024 * 1024)
+int ozk_matmul_f64_noalloc(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
+                           int64_t ldc, int64_t N, int64_t K, int64_t M, int n_hi, int n_lo,
+                           int32_t* status_dev, void* stream);
+
 /* The FP64 host pipeline (matmul(pipeline='host'), ozaki_jax/matmul.py:823-851):
  * FP64 extraction into n_slices slices, triangular pairs, FP64 accumulation,
  * all on the device.  rho < 0 selects _compute_rho(K). */

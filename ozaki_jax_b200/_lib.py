@@ -53,6 +53,8 @@ SIGNATURES = {
     "ozk_matmul_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_int, c_int]),
     "ozk_matmul_f64": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64, c_int, c_int,
                                c_int, c_int, vp, c_size, vp, vp]),
+    "ozk_matmul_f64_noalloc": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64,
+                                       c_int, c_int, vp, vp]),
     "ozk_matmul_host_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_int]),
     "ozk_matmul_host_f64": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64, c_int,
                                     c_int, vp, c_size, vp, vp]),

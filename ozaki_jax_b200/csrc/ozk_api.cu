@@ -101,6 +101,7 @@ struct Workspace {
   uint16_t* SB;
   int32_t* eA;
   int32_t* eB;
+  double* BT;  // transposed FP64 copy of the column-extracted operand
   float* products;
   size_t bytes;
 };
@@ -108,8 +109,9 @@ struct Workspace {
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // Layout: SA [nS][N][k_pad] | SB [nS][M][k_pad] | eA [nS][N] | eB [nS][M] |
-// products [n_pairs][N][M] (only when materialised).
-static Workspace layout(void* base, int64_t N, int64_t K, int64_t M, int nS, int n_prod) {
+// BT [bt_elems] FP64 | products [n_pairs][N][M] (only when materialised).
+static Workspace layout(void* base, int64_t N, int64_t K, int64_t M, int nS, int n_prod,
+                        int64_t bt_elems) {
   const int64_t k_pad = round_up(K < 1 ? 1 : K, OZK_KB);
   Workspace w;
   size_t off = 0;
@@ -122,6 +124,8 @@ static Workspace layout(void* base, int64_t N, int64_t K, int64_t M, int nS, int
   off += align256((size_t)nS * N * 4);
   w.eB = (int32_t*)(b + off);
   off += align256((size_t)nS * M * 4);
+  w.BT = (double*)(b + off);
+  off += align256((size_t)bt_elems * 8);
   w.products = (float*)(b + off);
   off += align256((size_t)n_prod * N * M * 4);
   w.bytes = off;
@@ -209,8 +213,14 @@ int ozk_extract_cols_f64(const double* X, int64_t ldx, int64_t K, int64_t cols, 
   int rc = check_extract_args(X, ldx, cols, K, cols, n_hi, n_lo, slices, k_pad, exps);
   if (rc) return rc;
   if (rho < 0) rho = rho_f32(K);
+  // The transposed fast path needs a cols x K FP64 scratch from the pool.
+  ScopedWs ws;
+  double* scratch = nullptr;
+  if (k_pad <= 65536 && cols > 0 &&
+      ws.acquire(nullptr, 0, (size_t)cols * K * 8, (cudaStream_t)stream) == OZK_OK)
+    scratch = (double*)ws.ptr;
   return launch_extract_cols(X, ldx, K, cols, rho, n_hi, n_lo, slices, k_pad, exps, status_dev,
-                             (cudaStream_t)stream);
+                             scratch, (cudaStream_t)stream);
 }
 
 int ozk_extract_rows_host_f64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
@@ -263,12 +273,12 @@ int ozk_accumulate_2sum(const float* products, const int32_t* eA, const int32_t*
 }
 
 size_t ozk_matmul_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo) {
-  return layout(nullptr, N, K, M, n_hi + n_lo, 0).bytes;
+  return layout(nullptr, N, K, M, n_hi + n_lo, 0, M * K).bytes;
 }
 
 static size_t matmul_ws_bytes_mode(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo, int mode) {
   int n_prod = mode == OZK_ACC_PRODUCTS ? n_hi * n_hi + 2 * n_hi * n_lo : 0;
-  return layout(nullptr, N, K, M, n_hi + n_lo, n_prod).bytes;
+  return layout(nullptr, N, K, M, n_hi + n_lo, n_prod, M * K).bytes;
 }
 
 int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
@@ -293,10 +303,11 @@ int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, d
   size_t need = matmul_ws_bytes_mode(N, K, M, n_hi, n_lo, acc_mode);
   ScopedWs ws;
   if ((rc = ws.acquire(workspace, ws_bytes, need, s))) return rc;
-  Workspace w = layout(ws.ptr, N, K, M, nS, acc_mode == OZK_ACC_PRODUCTS ? np : 0);
+  Workspace w = layout(ws.ptr, N, K, M, nS, acc_mode == OZK_ACC_PRODUCTS ? np : 0, M * K);
   if ((rc = launch_extract_rows(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
     return rc;
-  if ((rc = launch_extract_cols(B, ldb, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, s)))
+  if ((rc = launch_extract_cols(B, ldb, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, w.BT,
+                                s)))
     return rc;
   if (acc_mode == OZK_ACC_F64)
     return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np, OZK_ACC_F64,
@@ -310,7 +321,7 @@ int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, d
 }
 
 size_t ozk_matmul_host_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_slices) {
-  return layout(nullptr, N, K, M, n_slices, 0).bytes;
+  return layout(nullptr, N, K, M, n_slices, 0, 0).bytes;
 }
 
 int ozk_matmul_host_f64(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
@@ -336,7 +347,7 @@ int ozk_matmul_host_f64(const double* A, int64_t lda, const double* B, int64_t l
   ScopedWs ws;
   if ((rc = ws.acquire(workspace, ws_bytes, ozk_matmul_host_workspace_bytes(N, K, M, n_slices), s)))
     return rc;
-  Workspace w = layout(ws.ptr, N, K, M, n_slices, 0);
+  Workspace w = layout(ws.ptr, N, K, M, n_slices, 0, 0);
   if ((rc = launch_extract_rows64(A, lda, N, K, rho, n_slices, w.SA, k_pad, w.eA, status_dev, s)))
     return rc;
   if ((rc = launch_extract_cols64(B, ldb, K, M, rho, n_slices, w.SB, k_pad, w.eB, status_dev, s)))
@@ -349,7 +360,7 @@ int ozk_matmul_host_f64(const double* A, int64_t lda, const double* B, int64_t l
 // the N rows -- both the row extraction of A^T and the column extraction of
 // A in the reference (gram.py:22-35), which coincide.
 size_t ozk_gram_workspace_bytes(int64_t N, int64_t K, int n_hi, int n_lo) {
-  return layout(nullptr, K, N, 0, n_hi + n_lo, 0).bytes;
+  return layout(nullptr, K, N, 0, n_hi + n_lo, 0, K * N).bytes;
 }
 
 int ozk_gram_f64(const double* A, int64_t lda, double* G, int64_t ldg, int64_t N, int64_t K,
@@ -371,15 +382,16 @@ int ozk_gram_f64(const double* A, int64_t lda, double* G, int64_t ldg, int64_t N
   ScopedWs ws;
   if ((rc = ws.acquire(workspace, ws_bytes, ozk_gram_workspace_bytes(N, K, n_hi, n_lo), s)))
     return rc;
-  Workspace w = layout(ws.ptr, K, N, 0, nS, 0);
-  if ((rc = launch_extract_cols(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
+  Workspace w = layout(ws.ptr, K, N, 0, nS, 0, K * N);
+  if ((rc = launch_extract_cols(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, w.BT,
+                                s)))
     return rc;
   return launch_slice_gemm(w.SA, w.eA, nS, w.SA, w.eA, nS, K, K, k_pad, pa, pb, np, OZK_ACC_F64, 1,
                            1.0, 0.0, nullptr, 0, G, ldg, nullptr, status_dev, s);
 }
 
 size_t ozk_residual_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo) {
-  return layout(nullptr, N, K, M, n_hi + n_lo, 0).bytes;
+  return layout(nullptr, N, K, M, n_hi + n_lo, 0, M * K).bytes;
 }
 
 int ozk_residual_f64(const double* A, int64_t lda, const double* X, int64_t ldx, const double* Bv,
@@ -403,10 +415,11 @@ int ozk_residual_f64(const double* A, int64_t lda, const double* X, int64_t ldx,
   ScopedWs ws;
   if ((rc = ws.acquire(workspace, ws_bytes, ozk_residual_workspace_bytes(N, K, M, n_hi, n_lo), s)))
     return rc;
-  Workspace w = layout(ws.ptr, N, K, M, nS, 0);
+  Workspace w = layout(ws.ptr, N, K, M, nS, 0, M * K);
   if ((rc = launch_extract_rows(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
     return rc;
-  if ((rc = launch_extract_cols(X, ldx, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, s)))
+  if ((rc = launch_extract_cols(X, ldx, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, w.BT,
+                                s)))
     return rc;
   return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np, OZK_ACC_F64, 0,
                            -1.0, 1.0, Bv, ldb, R, ldr, nullptr, status_dev, s);

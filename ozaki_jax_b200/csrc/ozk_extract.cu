@@ -166,6 +166,159 @@ __global__ void __launch_bounds__(NT) k_extract_rows(const double* __restrict__ 
   }
 }
 
+// ---------------------------------------------------------------- rows, register resident
+
+// One line per CTA (or per cluster of CL CTAs that split K), the split FP32
+// residuals held in registers: the line is read from DRAM once and every
+// slice costs one block (and cluster) max-reduction followed by an in-register
+// update that emits the slice (columns K..k_pad-1 are written as zeros).
+// Thread `tid` owns the column pairs
+// kbase + 2*(p*256 + tid) + {0,1}, p < EPT/2, so the loads are 16-byte vectors
+// and the slice stores 4-byte words, both coalesced.  Line maxima are shared
+// across the cluster through distributed shared memory.
+constexpr int kRegNT = 256;
+
+template <int EPT, int CL>
+__global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
+    const double* __restrict__ X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
+    int n_lo, uint16_t* __restrict__ slices, int64_t k_pad, int32_t* __restrict__ exps,
+    int32_t* status, int vec) {
+  static_assert(EPT % 2 == 0, "EPT must be even");
+  __shared__ float s_part[2][2][kRegNT / 32];  // [parity][hi, lo][warp]
+  __shared__ float s_cta[2][2];                // [parity][hi, lo] CTA maxima for the cluster
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t crank = CL > 1 ? cluster_ctarank() : 0;
+  const int64_t kbase = (int64_t)crank * kRegNT * EPT;
+  const int npass = n_hi > n_lo ? n_hi : n_lo;
+  const int64_t slice_stride = rows * k_pad;
+  uint32_t g = 0;  // running slice counter: parity of the reduction buffers
+
+  for (int64_t row = blockIdx.x / CL; row < rows; row += gridDim.x / CL) {
+    const double* x = X + row * ldx;
+    float rh[EPT], rl[EPT];
+    int32_t flags = 0;
+#pragma unroll
+    for (int p = 0; p < EPT / 2; ++p) {
+      const int64_t k = kbase + 2 * ((int64_t)p * kRegNT + tid);
+      double x0 = 0.0, x1 = 0.0;
+      if (vec && k + 1 < K) {
+        double2 v2 = __ldg(reinterpret_cast<const double2*>(x + k));
+        x0 = v2.x;
+        x1 = v2.y;
+      } else {
+        if (k < K) x0 = __ldg(x + k);
+        if (k + 1 < K) x1 = __ldg(x + k + 1);
+      }
+      split_f64(x0, rh[2 * p], rl[2 * p]);
+      split_f64(x1, rh[2 * p + 1], rl[2 * p + 1]);
+      flags |= check_value(x0, rh[2 * p]) | check_value(x1, rh[2 * p + 1]);
+    }
+    if (flags) raise_flag(status, flags);
+
+    for (int t = 0; t < npass; ++t, ++g) {
+      const int par = g & 1;
+      const bool do_hi = t < n_hi, do_lo = t < n_lo;
+      float mh = 0.0f, ml = 0.0f;
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) {
+        mh = fmaxf(mh, fabsf(rh[e]));
+        ml = fmaxf(ml, fabsf(rl[e]));
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
+        ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, o));
+      }
+      if (lane == 0) {
+        s_part[par][0][warp] = mh;
+        s_part[par][1][warp] = ml;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int w = 0; w < kRegNT / 32; ++w) {
+        mh = fmaxf(mh, s_part[par][0][w]);
+        ml = fmaxf(ml, s_part[par][1][w]);
+      }
+      if constexpr (CL > 1) {
+        if (tid == 0) {
+          s_cta[par][0] = mh;
+          s_cta[par][1] = ml;
+        }
+        cluster_sync();
+        for (uint32_t r = 0; r < (uint32_t)CL; ++r) {
+          mh = fmaxf(mh, ld_dsmem_f32(&s_cta[par][0], r));
+          ml = fmaxf(ml, ld_dsmem_f32(&s_cta[par][1], r));
+        }
+      }
+      float sh = 0.f, ih = 0.f, sl = 0.f, il = 0.f;
+      int zh = 1, zl = 1, ch = 0, cl = 0;
+      if (do_hi) slice_params(mh, rho, sh, ih, zh, ch);
+      if (do_lo) slice_params(ml, rho, sl, il, zl, cl);
+      if (crank == 0 && tid == 0) {
+        if (do_hi) exps[(int64_t)t * rows + row] = ch;
+        if (do_lo) exps[(int64_t)(n_hi + t) * rows + row] = cl;
+      }
+      uint16_t* out_h = slices + (int64_t)t * slice_stride + row * k_pad;
+      uint16_t* out_l = slices + (int64_t)(n_hi + t) * slice_stride + row * k_pad;
+#pragma unroll
+      for (int p = 0; p < EPT / 2; ++p) {
+        const int64_t k = kbase + 2 * ((int64_t)p * kRegNT + tid);
+        if (do_hi) {
+          uint32_t w = 0;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float& r = rh[2 * p + h];
+            float v = zh ? 0.0f : __fsub_rn(__fadd_rn(r, sh), sh);
+            r = __fsub_rn(r, v);
+            if (k + h < K) w |= (uint32_t)bf16_bits_exact(__fmul_rn(v, ih)) << (16 * h);
+          }
+          if (k < k_pad) *reinterpret_cast<uint32_t*>(out_h + k) = w;
+        }
+        if (do_lo) {
+          uint32_t w = 0;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float& r = rl[2 * p + h];
+            float v = zl ? 0.0f : __fsub_rn(__fadd_rn(r, sl), sl);
+            r = __fsub_rn(r, v);
+            if (k + h < K) w |= (uint32_t)bf16_bits_exact(__fmul_rn(v, il)) << (16 * h);
+          }
+          if (k < k_pad) *reinterpret_cast<uint32_t*>(out_l + k) = w;
+        }
+      }
+    }
+  }
+  if constexpr (CL > 1) cluster_sync();  // peers may still read this CTA's s_cta
+}
+
+// ---------------------------------------------------------------- transpose
+
+// XT (cols x rows, leading dimension rows) = X^T for X (rows x cols, ldx):
+// 32 x 32 tiles through shared memory, both sides coalesced.
+__global__ void __launch_bounds__(256) k_transpose_f64(const double* __restrict__ X, int64_t ldx,
+                                                       int64_t rows, int64_t cols,
+                                                       double* __restrict__ XT) {
+  __shared__ double tile[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int64_t tr = blockIdx.y; tr * 32 < rows; tr += gridDim.y) {
+    for (int64_t tc = blockIdx.x; tc * 32 < cols; tc += gridDim.x) {
+      const int64_t r0 = tr * 32, c0 = tc * 32;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        int64_t r = r0 + ty + 8 * i, c = c0 + tx;
+        if (r < rows && c < cols) tile[ty + 8 * i][tx] = __ldg(X + r * ldx + c);
+      }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        int64_t c = c0 + ty + 8 * i, r = r0 + tx;
+        if (r < rows && c < cols) XT[c * rows + r] = tile[tx][ty + 8 * i];
+      }
+      __syncthreads();
+    }
+  }
+}
+
 // ---------------------------------------------------------------- columns
 
 // A block owns 32 adjacent columns (lane = column) and all K rows; its 8
@@ -477,6 +630,32 @@ int upload_log2_table(int dev) {
   return OZK_OK;
 }
 
+template <int EPT, int CL>
+static int launch_rows_reg(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
+                           int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                           int32_t* status, int dev, cudaStream_t stream) {
+  const int vec = (((uintptr_t)X & 15) == 0) && (ldx % 2 == 0);
+  // Enough lines in flight per SM to cover the reduction latencies.
+  int64_t per_sm = EPT <= 8 ? 8 : (EPT <= 16 ? 6 : 3);
+  int64_t clusters = (int64_t)device_sm_count(dev) * per_sm / CL;
+  if (clusters > rows) clusters = rows;
+  if (clusters < 1) clusters = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(clusters * CL));
+  cfg.blockDim = dim3(kRegNT);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_extract_rows_reg<EPT, CL>, X, ldx, rows, K, rho, n_hi,
+                                     n_lo, slices, k_pad, exps, status, vec);
+  return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows_reg launch", e);
+}
+
 int launch_extract_rows(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
                         cudaStream_t stream) {
@@ -485,25 +664,56 @@ int launch_extract_rows(const double* X, int64_t ldx, int64_t rows, int64_t K, i
   cudaGetDevice(&dev);
   int rc = upload_log2_table(dev);
   if (rc) return rc;
-  // Keep the lines in flight within a few tens of MB so passes 2.. hit L2.
+  // Register-resident path: one CTA covers 256*EPT columns, a cluster of up to
+  // 8 CTAs covers k_pad <= 65536.
+  if (k_pad <= 512)
+    return launch_rows_reg<2, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+  if (k_pad <= 1024)
+    return launch_rows_reg<4, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+  if (k_pad <= 2048)
+    return launch_rows_reg<8, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+  if (k_pad <= 4096)
+    return launch_rows_reg<16, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+  if (k_pad <= 8192)
+    return launch_rows_reg<32, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+  if (k_pad <= 16384)
+    return launch_rows_reg<32, 2>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+  if (k_pad <= 32768)
+    return launch_rows_reg<32, 4>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+  if (k_pad <= 65536)
+    return launch_rows_reg<32, 8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+  // Longer lines: multi-pass kernel (passes 2.. re-read the line from L2).
   int sms = device_sm_count(dev);
-  int64_t per_sm = K <= 4096 ? 8 : (K <= 16384 ? 4 : 2);
-  int64_t grid = rows < sms * per_sm ? rows : sms * per_sm;
-  if (K > 8192) {
-    k_extract_rows<512><<<(unsigned)grid, 512, 0, stream>>>(X, ldx, rows, K, rho, n_hi, n_lo,
-                                                             slices, k_pad, exps, status);
-  } else {
-    k_extract_rows<256><<<(unsigned)grid, 256, 0, stream>>>(X, ldx, rows, K, rho, n_hi, n_lo,
-                                                             slices, k_pad, exps, status);
-  }
+  int64_t grid = rows < sms * 2 ? rows : sms * 2;
+  k_extract_rows<512><<<(unsigned)grid, 512, 0, stream>>>(X, ldx, rows, K, rho, n_hi, n_lo, slices,
+                                                           k_pad, exps, status);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows launch", e);
 }
 
+int launch_transpose_f64(const double* X, int64_t ldx, int64_t rows, int64_t cols, double* XT,
+                         cudaStream_t stream) {
+  if (rows == 0 || cols == 0) return OZK_OK;
+  int64_t gx = (cols + 31) / 32, gy = (rows + 31) / 32;
+  if (gx > 65535) gx = 65535;
+  if (gy > 65535) gy = 65535;
+  k_transpose_f64<<<dim3((unsigned)gx, (unsigned)gy), 256, 0, stream>>>(X, ldx, rows, cols, XT);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OZK_OK : set_cuda_error("k_transpose_f64 launch", e);
+}
+
 int launch_extract_cols(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho, int n_hi,
                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
-                        cudaStream_t stream) {
+                        double* scratch, cudaStream_t stream) {
   if (cols == 0) return OZK_OK;
+  // Fast path: transpose into the caller's scratch (cols x K FP64), then the
+  // register-resident row kernel on the transposed lines.
+  if (scratch && k_pad <= 65536) {
+    int rc = launch_transpose_f64(X, ldx, K, cols, scratch, stream);
+    if (rc) return rc;
+    return launch_extract_rows(scratch, K, cols, K, rho, n_hi, n_lo, slices, k_pad, exps, status,
+                               stream);
+  }
   int dev;
   cudaGetDevice(&dev);
   int rc = upload_log2_table(dev);

@@ -25,9 +25,13 @@ inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 int launch_extract_rows(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
                         cudaStream_t stream);
+// scratch: cols x K FP64 buffer for the transposed fast path (NULL selects the
+// multi-pass column kernel).
 int launch_extract_cols(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho, int n_hi,
                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
-                        cudaStream_t stream);
+                        double* scratch, cudaStream_t stream);
+int launch_transpose_f64(const double* X, int64_t ldx, int64_t rows, int64_t cols, double* XT,
+                         cudaStream_t stream);
 int launch_extract_rows64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int ns,
                           uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
                           cudaStream_t stream);

@@ -192,6 +192,8 @@ def ours(args):
     SB = torch.empty((nS, m, k_pad), dtype=torch.int16, device=dev)
     eA = torch.empty((nS, nb), dtype=torch.int32, device=dev)
     eB = torch.empty((nS, m), dtype=torch.int32, device=dev)
+    BT = torch.empty((m, k), dtype=torch.float64, device=dev)  # transposed-B scratch
+    GW = torch.empty(lib.ozk_slice_gemm_workspace_bytes(), dtype=torch.uint8, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     pa = (ctypes.c_uint8 * 256)()
     pb = (ctypes.c_uint8 * 256)()
@@ -207,13 +209,14 @@ def ours(args):
                                             status.data_ptr(), sh))
         _lib.check(lib.ozk_extract_cols_f64(Bd.data_ptr(), m, k, m, rho, n_hi, n_lo,
                                             SB.data_ptr(), k_pad, eB.data_ptr(),
+                                            BT.data_ptr(), BT.numel() * 8,
                                             status.data_ptr(), sh))
         if evs:
             evs[1].record(stream)
         _lib.check(lib.ozk_slice_gemm(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(),
                                       eB.data_ptr(), nS, nb, m, k_pad, pa, pb, npairs,
                                       _lib.OZK_ACC_F64, 0, 1.0, 0.0, None, 0, C.data_ptr(), m,
-                                      None, status.data_ptr(), sh))
+                                      None, GW.data_ptr(), GW.numel(), status.data_ptr(), sh))
         if evs:
             evs[2].record(stream)
 
@@ -246,6 +249,14 @@ def ours(args):
         t = torch.tensor([total_ms, gemm_ms, extract_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms, gemm_ms, extract_ms = t.tolist()
+    gemm_waits = None
+    if os.environ.get("OZK_GEMM_STATS") == "1":
+        w = (ctypes.c_ulonglong * 4)()
+        n_ctas = lib.ozk_gemm_stats(w)
+        if n_ctas > 0 and w[3]:
+            gemm_waits = {"mma_wait_accumulator": w[0] / w[3], "mma_wait_loads": w[1] / w[3],
+                          "producer_wait_free_stage_cycles_per_cta": w[2] / n_ctas,
+                          "mma_total_cycles_per_cta": w[3] / n_ctas}
     ms_step = total_ms / args.steps
     flops_fp64eq = 2.0 * n * k * m
     value = flops_fp64eq / (ms_step * 1e-3) / 1e12
@@ -303,6 +314,7 @@ def ours(args):
             "rel_err": rel_err,
             "dgemm_fp64_tflops": dgemm_tflops_rank * world,
             "breakdown_ms": {"extract": extract_ms, "slice_gemm": gemm_ms},
+            "gemm_wait_fractions": gemm_waits,
             "roofline": {"bound": "tensor", "kernel": "k_slice_gemm",
                          "achieved": gemm_tflops, "peak": bf16_peak, "unit": "TFLOP/s",
                          "frac": gemm_tflops / bf16_peak, "peak_source": f"{src} sustained bf16",
@@ -318,7 +330,7 @@ def ours(args):
                     "h2d_bytes_per_step": int(8 * (nb * k + k * m)),
                     "d2h_bytes_per_step": int(8 * nb * m)},
             "clocks": clk,
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": 4 * args.steps,
         }
         print(json.dumps(out), flush=True)
     if world > 1:

@@ -80,10 +80,13 @@ int ozk_extract_rows_f64(const double* X, int64_t ldx, int64_t rows, int64_t K, 
 
 /* Column extraction of X (K x cols, ldx) (jax_extract_split_cols,
  * ozaki_jax/extract.py:245-286), written transposed: slices
- * [n_hi+n_lo][cols][k_pad] (K contiguous), exps [n_hi+n_lo][cols]. */
+ * [n_hi+n_lo][cols][k_pad] (K contiguous), exps [n_hi+n_lo][cols].
+ * scratch: optional device buffer of cols*K doubles for the transposed fast
+ * path (NULL: taken from the stream-ordered pool). */
 int ozk_extract_cols_f64(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho,
                          int n_hi, int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps,
-                         int32_t* status_dev, void* stream);
+                         double* scratch, size_t scratch_bytes, int32_t* status_dev,
+                         void* stream);
 
 /* FP64 sigma-trick extraction of the host pipeline (extract_split_rows /
  * extract_split_cols, ozaki_jax/extract.py:21-103): n_slices slices of the
@@ -109,12 +112,19 @@ int ozk_extract_cols_host_f64(const double* X, int64_t ldx, int64_t K, int64_t c
  * mode OZK_ACC_PRODUCTS: products[p][r][c] = P_p[r][c] (FP32, exact), ld = M.
  * symmetric != 0 (gram): requires SA == SB, eA == eB, N == M; only tiles on
  * or above the diagonal are computed and each is also written mirrored, so C
- * is exactly symmetric. */
+ * is exactly symmetric.
+ * workspace: optional device scratch of ozk_slice_gemm_workspace_bytes()
+ * bytes (256-byte aligned). */
 int ozk_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t* SB,
                    const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
                    const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
                    int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
-                   double* C, int64_t ldc, float* products, int32_t* status_dev, void* stream);
+                   double* C, int64_t ldc, float* products, void* workspace, size_t ws_bytes,
+                   int32_t* status_dev, void* stream);
+/* Scratch ozk_slice_gemm uses for its 256-wide tiles (per-CTA FP64 running
+ * sums, L2-resident); with a smaller or NULL workspace it runs 128-wide tiles
+ * that keep the sums in TMEM. */
+size_t ozk_slice_gemm_workspace_bytes(void);
 
 /* Reference-order FP32 2Sum accumulation of materialised products
  * (accumulate_2sum / _accumulate_2sum_logic, ozaki_jax/pallas_ops.py:178-239,
@@ -128,8 +138,9 @@ int ozk_accumulate_2sum(const float* products, const int32_t* eA, const int32_t*
 
 /* ---------------------------------------------------------------- pipelines */
 
-/* Workspace bytes ozk_matmul_f64 needs for an N x K by K x M product with
- * (n_hi, n_lo) slices. */
+/* Workspace bytes ozk_matmul_f64 uses for an N x K by K x M product with
+ * (n_hi, n_lo) slices on the current device.  A smaller workspace down to the
+ * slices-only size is accepted and selects 128-wide GEMM tiles. */
 size_t ozk_matmul_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo);
 
 /* The on-device pipeline (_matmul_ondevice accumulation='fused' /
@@ -195,6 +206,12 @@ int ozk_check_status(const int32_t* status_dev, void* stream);
 const char* ozk_strerror(int status);
 /* Copies the last error detail of the calling host thread into buf. */
 int ozk_last_error_detail(char* buf, size_t len);
+/* Diagnostics (no counterpart in the reference): with OZK_GEMM_STATS=1 in
+ * the environment, sums over the CTAs of the last slice-GEMM launch of
+ * {MMA-thread cycles waiting for a free accumulator, MMA-thread cycles waiting
+ * for loaded stages, producer cycles waiting for free stages, MMA-thread total
+ * cycles}; returns the CTA count (synchronises the device). */
+int ozk_gemm_stats(unsigned long long* out4);
 /* Library version string. */
 const char* ozk_version(void);
 

@@ -41,13 +41,15 @@ SIGNATURES = {
     "ozk_extract_rows_f64": (c_int, [vp, c_i64, c_i64, c_i64, c_int, c_int, c_int, vp, c_i64, vp,
                                      vp, vp]),
     "ozk_extract_cols_f64": (c_int, [vp, c_i64, c_i64, c_i64, c_int, c_int, c_int, vp, c_i64, vp,
-                                     vp, vp]),
+                                     vp, c_size, vp, vp]),
     "ozk_extract_rows_host_f64": (c_int, [vp, c_i64, c_i64, c_i64, c_int, c_int, vp, c_i64, vp,
                                           vp, vp]),
     "ozk_extract_cols_host_f64": (c_int, [vp, c_i64, c_i64, c_i64, c_int, c_int, vp, c_i64, vp,
                                           vp, vp]),
     "ozk_slice_gemm": (c_int, [vp, vp, c_int, vp, vp, c_int, c_i64, c_i64, c_i64, vp, vp, c_int,
-                               c_int, c_int, c_dbl, c_dbl, vp, c_i64, vp, c_i64, vp, vp, vp]),
+                               c_int, c_int, c_dbl, c_dbl, vp, c_i64, vp, c_i64, vp, vp, c_size,
+                               vp, vp]),
+    "ozk_slice_gemm_workspace_bytes": (c_size, []),
     "ozk_accumulate_2sum": (c_int, [vp, vp, vp, c_i64, c_i64, c_int, c_int, vp, vp, vp, c_i64,
                                     vp]),
     "ozk_matmul_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_int, c_int]),
@@ -65,6 +67,7 @@ SIGNATURES = {
     "ozk_residual_f64": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64,
                                  c_int, c_int, c_int, vp, c_size, vp, vp]),
     "ozk_check_status": (c_int, [vp, vp]),
+    "ozk_gemm_stats": (c_int, [vp]),
     "ozk_strerror": (ctypes.c_char_p, [c_int]),
     "ozk_last_error_detail": (c_int, [ctypes.c_char_p, c_size]),
     "ozk_version": (ctypes.c_char_p, []),

@@ -103,15 +103,18 @@ struct Workspace {
   int32_t* eB;
   double* BT;  // transposed FP64 copy of the column-extracted operand
   float* products;
+  double* state;  // per-CTA FP64 running sums of the 256-wide GEMM tiles
+  size_t state_bytes;
   size_t bytes;
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // Layout: SA [nS][N][k_pad] | SB [nS][M][k_pad] | eA [nS][N] | eB [nS][M] |
-// BT [bt_elems] FP64 | products [n_pairs][N][M] (only when materialised).
+// BT [bt_elems] FP64 | products [n_pairs][N][M] (only when materialised) |
+// state [state_bytes] (optional GEMM scratch).
 static Workspace layout(void* base, int64_t N, int64_t K, int64_t M, int nS, int n_prod,
-                        int64_t bt_elems) {
+                        int64_t bt_elems, size_t state_bytes = 0) {
   const int64_t k_pad = round_up(K < 1 ? 1 : K, OZK_KB);
   Workspace w;
   size_t off = 0;
@@ -128,6 +131,9 @@ static Workspace layout(void* base, int64_t N, int64_t K, int64_t M, int nS, int
   off += align256((size_t)bt_elems * 8);
   w.products = (float*)(b + off);
   off += align256((size_t)n_prod * N * M * 4);
+  w.state = state_bytes ? (double*)(b + off) : nullptr;
+  w.state_bytes = state_bytes;
+  off += align256(state_bytes);
   w.bytes = off;
   return w;
 }
@@ -155,6 +161,28 @@ struct ScopedWs {
     if (owned && ptr) cudaFreeAsync(ptr, s);
   }
 };
+
+static size_t cur_state_bytes() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return gemm_state_bytes(dev);
+}
+
+// Workspace actually usable: the full size when given (or pool-allocated),
+// else the minimum without the GEMM state scratch.
+static int pick_workspace(void* given, size_t given_bytes, size_t full, size_t minimum,
+                          bool& with_state) {
+  with_state = true;
+  if (!given) return OZK_OK;
+  if (given_bytes >= full) return OZK_OK;
+  with_state = false;
+  if (given_bytes >= minimum) return OZK_OK;
+  return set_error(OZK_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", given_bytes, minimum);
+}
+
+size_t matmul_min_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo) {
+  return layout(nullptr, N, K, M, n_hi + n_lo, 0, M * K).bytes;
+}
 
 }  // namespace ozk
 
@@ -208,16 +236,18 @@ int ozk_extract_rows_f64(const double* X, int64_t ldx, int64_t rows, int64_t K, 
 }
 
 int ozk_extract_cols_f64(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho, int n_hi,
-                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps,
-                         int32_t* status_dev, void* stream) {
+                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps, double* scratch,
+                         size_t scratch_bytes, int32_t* status_dev, void* stream) {
   int rc = check_extract_args(X, ldx, cols, K, cols, n_hi, n_lo, slices, k_pad, exps);
   if (rc) return rc;
   if (rho < 0) rho = rho_f32(K);
-  // The transposed fast path needs a cols x K FP64 scratch from the pool.
+  const size_t need = (size_t)cols * K * 8;
+  if (scratch && scratch_bytes < need)
+    return set_error(OZK_ERR_WORKSPACE, "scratch %zu bytes < %zu needed", scratch_bytes, need);
+  // The transposed fast path needs a cols x K FP64 scratch (caller's or pool).
   ScopedWs ws;
-  double* scratch = nullptr;
-  if (k_pad <= 65536 && cols > 0 &&
-      ws.acquire(nullptr, 0, (size_t)cols * K * 8, (cudaStream_t)stream) == OZK_OK)
+  if (!scratch && k_pad <= 65536 && cols > 0 &&
+      ws.acquire(nullptr, 0, need, (cudaStream_t)stream) == OZK_OK)
     scratch = (double*)ws.ptr;
   return launch_extract_cols(X, ldx, K, cols, rho, n_hi, n_lo, slices, k_pad, exps, status_dev,
                              scratch, (cudaStream_t)stream);
@@ -251,16 +281,21 @@ int ozk_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t
                    const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
                    const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
                    int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
-                   double* C, int64_t ldc, float* products, int32_t* status_dev, void* stream) {
+                   double* C, int64_t ldc, float* products, void* workspace, size_t ws_bytes,
+                   int32_t* status_dev, void* stream) {
   if (!SA || !SB || !eA || !eB || !pair_a || !pair_b) return set_error(OZK_ERR_ARG, "NULL pointer");
   if (N < 0 || M < 0) return set_error(OZK_ERR_ARG, "bad shape");
   if (mode == OZK_ACC_F64 && ldc < M) return set_error(OZK_ERR_ARG, "ldc < M");
   if (beta != 0.0 && ldcin < M) return set_error(OZK_ERR_ARG, "ldcin < M");
   if (alpha != 1.0 && alpha != -1.0) return set_error(OZK_ERR_ARG, "alpha must be +1 or -1");
+  if (workspace && ((uintptr_t)workspace & 255))
+    return set_error(OZK_ERR_ARG, "workspace not 256-byte aligned");
   return launch_slice_gemm(SA, eA, nA, SB, eB, nB, N, M, k_pad, pair_a, pair_b, n_pairs, mode,
-                           symmetric, alpha, beta, Cin, ldcin, C, ldc, products, status_dev,
-                           (cudaStream_t)stream);
+                           symmetric, alpha, beta, Cin, ldcin, C, ldc, products, (double*)workspace,
+                           workspace ? ws_bytes : 0, status_dev, (cudaStream_t)stream);
 }
+
+size_t ozk_slice_gemm_workspace_bytes(void) { return cur_state_bytes(); }
 
 int ozk_accumulate_2sum(const float* products, const int32_t* eA, const int32_t* eB, int64_t N,
                         int64_t M, int n_hi, int n_lo, float* C_hi, float* C_lo, double* C,
@@ -273,12 +308,14 @@ int ozk_accumulate_2sum(const float* products, const int32_t* eA, const int32_t*
 }
 
 size_t ozk_matmul_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo) {
-  return layout(nullptr, N, K, M, n_hi + n_lo, 0, M * K).bytes;
+  return layout(nullptr, N, K, M, n_hi + n_lo, 0, M * K, cur_state_bytes()).bytes;
 }
 
-static size_t matmul_ws_bytes_mode(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo, int mode) {
+static size_t matmul_ws_bytes_mode(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo, int mode,
+                                   bool with_state) {
   int n_prod = mode == OZK_ACC_PRODUCTS ? n_hi * n_hi + 2 * n_hi * n_lo : 0;
-  return layout(nullptr, N, K, M, n_hi + n_lo, n_prod, M * K).bytes;
+  return layout(nullptr, N, K, M, n_hi + n_lo, n_prod, M * K, with_state ? cur_state_bytes() : 0)
+      .bytes;
 }
 
 int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
@@ -300,28 +337,37 @@ int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, d
   cudaStream_t s = (cudaStream_t)stream;
   const int nS = n_hi + n_lo;
   const int64_t k_pad = round_up(K, OZK_KB);
-  size_t need = matmul_ws_bytes_mode(N, K, M, n_hi, n_lo, acc_mode);
+  const bool prod = acc_mode == OZK_ACC_PRODUCTS;
+  bool with_state;
+  if ((rc = pick_workspace(workspace, ws_bytes,
+                           matmul_ws_bytes_mode(N, K, M, n_hi, n_lo, acc_mode, !prod),
+                           matmul_ws_bytes_mode(N, K, M, n_hi, n_lo, acc_mode, false), with_state)))
+    return rc;
+  with_state = with_state && !prod;
+  size_t need = matmul_ws_bytes_mode(N, K, M, n_hi, n_lo, acc_mode, with_state);
   ScopedWs ws;
-  if ((rc = ws.acquire(workspace, ws_bytes, need, s))) return rc;
-  Workspace w = layout(ws.ptr, N, K, M, nS, acc_mode == OZK_ACC_PRODUCTS ? np : 0, M * K);
+  if ((rc = ws.acquire(workspace, workspace ? ws_bytes : need, need, s))) return rc;
+  Workspace w = layout(ws.ptr, N, K, M, nS, prod ? np : 0, M * K,
+                       with_state ? cur_state_bytes() : 0);
   if ((rc = launch_extract_rows(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
     return rc;
   if ((rc = launch_extract_cols(B, ldb, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, w.BT,
                                 s)))
     return rc;
-  if (acc_mode == OZK_ACC_F64)
+  if (!prod)
     return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np, OZK_ACC_F64,
-                             0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, status_dev, s);
+                             0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, w.state, w.state_bytes,
+                             status_dev, s);
   if ((rc = launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np,
                               OZK_ACC_PRODUCTS, 0, 1.0, 0.0, nullptr, 0, nullptr, 0, w.products,
-                              status_dev, s)))
+                              nullptr, 0, status_dev, s)))
     return rc;
   return launch_accumulate_2sum(w.products, w.eA, w.eB, N, M, n_hi, n_lo, nullptr, nullptr, C, ldc,
                                 s);
 }
 
 size_t ozk_matmul_host_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_slices) {
-  return layout(nullptr, N, K, M, n_slices, 0, 0).bytes;
+  return layout(nullptr, N, K, M, n_slices, 0, 0, cur_state_bytes()).bytes;
 }
 
 int ozk_matmul_host_f64(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
@@ -344,23 +390,29 @@ int ozk_matmul_host_f64(const double* A, int64_t lda, const double* B, int64_t l
   if (N == 0 || M == 0) return OZK_OK;
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t k_pad = round_up(K, OZK_KB);
-  ScopedWs ws;
-  if ((rc = ws.acquire(workspace, ws_bytes, ozk_matmul_host_workspace_bytes(N, K, M, n_slices), s)))
+  bool with_state;
+  if ((rc = pick_workspace(workspace, ws_bytes, ozk_matmul_host_workspace_bytes(N, K, M, n_slices),
+                           layout(nullptr, N, K, M, n_slices, 0, 0).bytes, with_state)))
     return rc;
-  Workspace w = layout(ws.ptr, N, K, M, n_slices, 0, 0);
+  const size_t sb = with_state ? cur_state_bytes() : 0;
+  const size_t need = layout(nullptr, N, K, M, n_slices, 0, 0, sb).bytes;
+  ScopedWs ws;
+  if ((rc = ws.acquire(workspace, workspace ? ws_bytes : need, need, s))) return rc;
+  Workspace w = layout(ws.ptr, N, K, M, n_slices, 0, 0, sb);
   if ((rc = launch_extract_rows64(A, lda, N, K, rho, n_slices, w.SA, k_pad, w.eA, status_dev, s)))
     return rc;
   if ((rc = launch_extract_cols64(B, ldb, K, M, rho, n_slices, w.SB, k_pad, w.eB, status_dev, s)))
     return rc;
   return launch_slice_gemm(w.SA, w.eA, n_slices, w.SB, w.eB, n_slices, N, M, k_pad, pa, pb, np,
-                           OZK_ACC_F64, 0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, status_dev, s);
+                           OZK_ACC_F64, 0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, w.state,
+                           w.state_bytes, status_dev, s);
 }
 
 // gram: the column extraction of A (N x K) gives, per column of A, slices over
 // the N rows -- both the row extraction of A^T and the column extraction of
 // A in the reference (gram.py:22-35), which coincide.
 size_t ozk_gram_workspace_bytes(int64_t N, int64_t K, int n_hi, int n_lo) {
-  return layout(nullptr, K, N, 0, n_hi + n_lo, 0, K * N).bytes;
+  return layout(nullptr, K, N, 0, n_hi + n_lo, 0, K * N, cur_state_bytes()).bytes;
 }
 
 int ozk_gram_f64(const double* A, int64_t lda, double* G, int64_t ldg, int64_t N, int64_t K,
@@ -379,19 +431,25 @@ int ozk_gram_f64(const double* A, int64_t lda, double* G, int64_t ldg, int64_t N
   cudaStream_t s = (cudaStream_t)stream;
   const int nS = n_hi + n_lo;
   const int64_t k_pad = round_up(N, OZK_KB);
-  ScopedWs ws;
-  if ((rc = ws.acquire(workspace, ws_bytes, ozk_gram_workspace_bytes(N, K, n_hi, n_lo), s)))
+  bool with_state;
+  if ((rc = pick_workspace(workspace, ws_bytes, ozk_gram_workspace_bytes(N, K, n_hi, n_lo),
+                           layout(nullptr, K, N, 0, nS, 0, K * N).bytes, with_state)))
     return rc;
-  Workspace w = layout(ws.ptr, K, N, 0, nS, 0, K * N);
+  const size_t sb = with_state ? cur_state_bytes() : 0;
+  const size_t need = layout(nullptr, K, N, 0, nS, 0, K * N, sb).bytes;
+  ScopedWs ws;
+  if ((rc = ws.acquire(workspace, workspace ? ws_bytes : need, need, s))) return rc;
+  Workspace w = layout(ws.ptr, K, N, 0, nS, 0, K * N, sb);
   if ((rc = launch_extract_cols(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, w.BT,
                                 s)))
     return rc;
   return launch_slice_gemm(w.SA, w.eA, nS, w.SA, w.eA, nS, K, K, k_pad, pa, pb, np, OZK_ACC_F64, 1,
-                           1.0, 0.0, nullptr, 0, G, ldg, nullptr, status_dev, s);
+                           1.0, 0.0, nullptr, 0, G, ldg, nullptr, w.state, w.state_bytes,
+                           status_dev, s);
 }
 
 size_t ozk_residual_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo) {
-  return layout(nullptr, N, K, M, n_hi + n_lo, 0, M * K).bytes;
+  return layout(nullptr, N, K, M, n_hi + n_lo, 0, M * K, cur_state_bytes()).bytes;
 }
 
 int ozk_residual_f64(const double* A, int64_t lda, const double* X, int64_t ldx, const double* Bv,
@@ -412,17 +470,23 @@ int ozk_residual_f64(const double* A, int64_t lda, const double* X, int64_t ldx,
   cudaStream_t s = (cudaStream_t)stream;
   const int nS = n_hi + n_lo;
   const int64_t k_pad = round_up(K, OZK_KB);
-  ScopedWs ws;
-  if ((rc = ws.acquire(workspace, ws_bytes, ozk_residual_workspace_bytes(N, K, M, n_hi, n_lo), s)))
+  bool with_state;
+  if ((rc = pick_workspace(workspace, ws_bytes, ozk_residual_workspace_bytes(N, K, M, n_hi, n_lo),
+                           layout(nullptr, N, K, M, nS, 0, M * K).bytes, with_state)))
     return rc;
-  Workspace w = layout(ws.ptr, N, K, M, nS, 0, M * K);
+  const size_t sb = with_state ? cur_state_bytes() : 0;
+  const size_t need = layout(nullptr, N, K, M, nS, 0, M * K, sb).bytes;
+  ScopedWs ws;
+  if ((rc = ws.acquire(workspace, workspace ? ws_bytes : need, need, s))) return rc;
+  Workspace w = layout(ws.ptr, N, K, M, nS, 0, M * K, sb);
   if ((rc = launch_extract_rows(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
     return rc;
   if ((rc = launch_extract_cols(X, ldx, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, w.BT,
                                 s)))
     return rc;
   return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np, OZK_ACC_F64, 0,
-                           -1.0, 1.0, Bv, ldb, R, ldr, nullptr, status_dev, s);
+                           -1.0, 1.0, Bv, ldb, R, ldr, nullptr, w.state, w.state_bytes, status_dev,
+                           s);
 }
 
 int ozk_check_status(const int32_t* status_dev, void* stream) {

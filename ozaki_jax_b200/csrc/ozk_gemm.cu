@@ -29,6 +29,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "ozk_device.cuh"
@@ -37,7 +38,6 @@
 namespace ozk {
 
 constexpr int kBM = 128;
-constexpr int kThreads = 192;
 
 struct PairList {
   uint8_t a[OZK_MAX_PAIRS];
@@ -61,18 +61,37 @@ struct GemmArgs {
   float* products;
   int32_t* status;
   uint64_t budget_ns;
+  unsigned long long* stats;  // optional per-CTA wait-cycle counters (diagnostics)
+  double* state;              // per-CTA FP64 running sums (BN = 256 tiles)
 };
 
-template <int BN>
+// PAIR = false: one CTA per output tile of 128 x BN.
+// PAIR = true:  a cluster of two CTAs (a CTA pair on one TPC) per 256 x BN
+//   tile with cta_group::2 MMAs (M = 256): each CTA stages its 128 rows of A
+//   and half of B's BN rows, so a pair moves 3/4 of the shared-memory bytes
+//   per FLOP that two single CTAs would; the even CTA issues the MMAs, its
+//   full barriers count both CTAs' TMA bytes, stage releases and
+//   accumulator-ready signals go to both CTAs, and both epilogues report to
+//   the even CTA's accumulator-empty barriers.
+template <int BN, bool PAIR>
 struct GemmCfg {
-  static constexpr int STAGES = BN >= 64 ? 6 : 8;
+  static constexpr int CTA_N = PAIR ? BN / 2 : BN;  // B rows staged per CTA
+  static constexpr int TILE_M = PAIR ? 2 * kBM : kBM;
   static constexpr int A_BYTES = kBM * OZK_KB * 2;
-  static constexpr int B_BYTES = BN * OZK_KB * 2;
+  static constexpr int B_BYTES = CTA_N * OZK_KB * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 4 * BN < 32 ? 32 : 4 * BN;
+  static constexpr int STAGES = BN >= 256 ? 6 : (PAIR ? 8 : (BN >= 64 ? 6 : 8));
+  // BN = 256: both TMEM accumulators take all 512 columns and the FP64 running
+  // sum lives in a per-CTA global scratch; otherwise it is kept in TMEM.
+  static constexpr bool GSTATE = BN >= 256;
+  static constexpr int TMEM_COLS = GSTATE ? 2 * BN : (4 * BN < 32 ? 32 : 4 * BN);
+  static constexpr int EPI_WARPS = GSTATE ? 8 : 4;  // 4 lane quadrants x column halves
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int EPI_COLS = BN / (EPI_WARPS / 4);  // columns per epilogue thread
   static constexpr int CH = BN < 32 ? BN : 32;  // epilogue column chunk
   static constexpr int EB_BYTES = OZK_MAX_SLICES * BN * 4;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EB_BYTES + 256;
+  static constexpr int64_t STATE_PER_CTA = (int64_t)kBM * BN;  // doubles
 };
 
 // Output tile of a linear tile index: group-of-rows raster for L2 reuse, or
@@ -95,11 +114,11 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& tm, i
   tn = r / gsz;
 }
 
-template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, bool PAIR>
+__global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
     k_slice_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                  const __grid_constant__ PairList pairs, const __grid_constant__ GemmArgs g) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int CH = Cfg::CH;
   extern __shared__ uint8_t smem_raw[];
@@ -117,6 +136,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* s_abort = (volatile int*)(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0;  // 0 = MMA-issuing CTA
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -125,15 +147,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);
-      mbar_init(&acce[i], 4);
+      mbar_init(&acce[i], (PAIR ? 2 : 1) * Cfg::EPI_WARPS);
     }
     mbar_init(mma_done, 1);
     *s_abort = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(s_tmem, Cfg::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR) tmem_alloc_pair(s_tmem, Cfg::TMEM_COLS);
+    else tmem_alloc(s_tmem, Cfg::TMEM_COLS);
+  }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // peer barriers initialised before any remote use
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
   const int npairs = pairs.n;
@@ -145,89 +171,130 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&mapB);
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
+      long long w_empty = 0;
+      for (int t = unit; ok && t < g.num_tiles; t += n_units) {
         int tm, tn;
         tile_coords(g, t, tm, tn);
+        const int arow = tm * Cfg::TILE_M + (int)rank * kBM;
+        const int brow = tn * BN + (int)rank * Cfg::CTA_N;
         for (int p = 0; ok && p < npairs; ++p) {
           const int a = pairs.a[p], b = pairs.b[p];
           for (int kb = 0; kb < g.num_kb; ++kb) {
             const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+            long long c0 = clock64();
             if (!mbar_wait(&empty[s], ph ^ 1, s_abort, g.status, g.budget_ns)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-            tma_load_3d(sA + s * Cfg::A_BYTES, &mapA, &full[s], kb * OZK_KB, tm * kBM, a);
-            tma_load_3d(sB + s * Cfg::B_BYTES, &mapB, &full[s], kb * OZK_KB, tn * BN, b);
+            w_empty += clock64() - c0;
+            if constexpr (PAIR) {
+              if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+              const uint32_t fb = mapa_u32(&full[s], 0);
+              tma_load_3d_pair(sA + s * Cfg::A_BYTES, &mapA, fb, kb * OZK_KB, arow, a);
+              tma_load_3d_pair(sB + s * Cfg::B_BYTES, &mapB, fb, kb * OZK_KB, brow, b);
+            } else {
+              mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+              tma_load_3d(sA + s * Cfg::A_BYTES, &mapA, &full[s], kb * OZK_KB, arow, a);
+              tma_load_3d(sB + s * Cfg::B_BYTES, &mapB, &full[s], kb * OZK_KB, brow, b);
+            }
             ++it;
           }
         }
       }
+      if (g.stats) g.stats[4 * blockIdx.x + 2] = (unsigned long long)w_empty;
       // Drain: every issued copy must land before shared memory is released.
-      uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0;
-      for (uint32_t j = first; j < it; ++j)
-        mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, g.status, g.budget_ns);
+      // (In a pair only the even CTA's full barriers count the bytes.)
+      if (!PAIR || rank == 0) {
+        uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0;
+        for (uint32_t j = first; j < it; ++j)
+          mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, g.status, g.budget_ns);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(Cfg::TILE_M, BN);
       uint32_t it = 0, acc_it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
+      long long w_acc = 0, w_full = 0, t_start = clock64();
+      for (int t = unit; ok && t < g.num_tiles; t += n_units) {
         for (int p = 0; ok && p < npairs; ++p) {
           const uint32_t buf = acc_it & 1, aph = (acc_it >> 1) & 1;
+          long long c0 = clock64();
           if (!mbar_wait(&acce[buf], aph ^ 1, s_abort, g.status, g.budget_ns)) {
             ok = false;
             break;
           }
+          w_acc += clock64() - c0;
           tc_fence_after();
           const uint32_t d = tmem + buf * BN;
           for (int kb = 0; kb < g.num_kb; ++kb) {
             const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+            long long c1 = clock64();
             if (!mbar_wait(&full[s], ph, s_abort, g.status, g.budget_ns)) {
               ok = false;
               break;
             }
+            w_full += clock64() - c1;
             tc_fence_after();
             const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES);
             const uint32_t b0 = smem_u32(sB + s * Cfg::B_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < OZK_KB / 16; ++kk)
-              umma_bf16(d, umma_desc_sw128(a0 + kk * 32), umma_desc_sw128(b0 + kk * 32), idesc,
-                        (kb | kk) != 0);
-            umma_commit(&empty[s]);
+            for (int kk = 0; kk < OZK_KB / 16; ++kk) {
+              const uint64_t da = umma_desc_sw128(a0 + kk * 32);
+              const uint64_t db = umma_desc_sw128(b0 + kk * 32);
+              if constexpr (PAIR) umma_bf16_pair(d, da, db, idesc, (kb | kk) != 0);
+              else umma_bf16(d, da, db, idesc, (kb | kk) != 0);
+            }
+            if constexpr (PAIR) umma_commit_pair(&empty[s], 0x3);
+            else umma_commit(&empty[s]);
             ++it;
           }
           if (!ok) break;
-          umma_commit(&accf[buf]);
+          if constexpr (PAIR) umma_commit_pair(&accf[buf], 0x3);
+          else umma_commit(&accf[buf]);
           ++acc_it;
         }
       }
       // All MMAs issued by this thread complete before TMEM is released.
-      umma_commit(mma_done);
+      if constexpr (PAIR) umma_commit_pair(mma_done, 0x1);
+      else umma_commit(mma_done);
       mbar_wait(mma_done, 0, nullptr, g.status, g.budget_ns);
+      if (g.stats) {
+        unsigned long long* st = g.stats + 4 * blockIdx.x;
+        st[0] = (unsigned long long)w_acc;
+        st[1] = (unsigned long long)w_full;
+        st[3] = (unsigned long long)(clock64() - t_start);
+      }
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    constexpr int NE = 32 * Cfg::EPI_WARPS;  // epilogue threads
     const int q = warp & 3;                 // TMEM lane quadrant of this warp
-    const int etid = threadIdx.x - 64;      // 0..127 among epilogue threads
+    const int half = (warp - 2) >> 2;       // column range of this warp
+    const int cbeg = half * Cfg::EPI_COLS;  // first tile column of this thread
+    const int etid = threadIdx.x - 64;      // 0..NE-1 among epilogue threads
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    // Column-major per-CTA FP64 state: a warp touches 32 consecutive rows of
+    // one column (256 contiguous bytes) per access.
+    double* const gst = Cfg::GSTATE ? g.state + (int64_t)blockIdx.x * Cfg::STATE_PER_CTA
+                                      + q * 32 + lane : nullptr;
+    const uint32_t acce_leader = PAIR ? mapa_u32(&acce[0], 0) : 0;
     uint32_t acc_it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
+    for (int t = unit; ok && t < g.num_tiles; t += n_units) {
       int tm, tn;
       tile_coords(g, t, tm, tn);
       const int64_t col0 = (int64_t)tn * BN;
-      named_bar(1, 128);
-      for (int e = etid; e < g.nB * BN; e += 128) {
+      named_bar(1, NE);
+      for (int e = etid; e < g.nB * BN; e += NE) {
         int64_t c = col0 + (e % BN);
         s_eB[e] = c < g.M ? g.eB[(int64_t)(e / BN) * g.M + c] : 0;
       }
-      named_bar(1, 128);
-      const int64_t row = (int64_t)tm * kBM + q * 32 + lane;
+      named_bar(1, NE);
+      const int64_t row = (int64_t)tm * Cfg::TILE_M + rank * kBM + q * 32 + lane;
       const bool rvalid = row < g.N;
       for (int p = 0; p < npairs; ++p) {
         const uint32_t buf = acc_it & 1, aph = (acc_it >> 1) & 1;
@@ -246,19 +313,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t t_lo = tmem + lane_base + 2 * BN;
         const uint32_t t_hi = tmem + lane_base + 3 * BN;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += CH) {
+        for (int c0 = cbeg; c0 < cbeg + Cfg::EPI_COLS; c0 += CH) {
           uint32_t P[CH], L[CH], H[CH];
           if constexpr (CH == 32) {
             tmem_ld32(t_acc + c0, P);
-            if (g.mode == OZK_ACC_F64 && !first) {
+            if (!Cfg::GSTATE && g.mode == OZK_ACC_F64 && !first) {
               tmem_ld32(t_lo + c0, L);
               tmem_ld32(t_hi + c0, H);
             }
           } else {
             tmem_ld16(t_acc + c0, P);
-            if (g.mode == OZK_ACC_F64 && !first) {
+            if (!Cfg::GSTATE && g.mode == OZK_ACC_F64 && !first) {
               tmem_ld16(t_lo + c0, L);
               tmem_ld16(t_hi + c0, H);
+            }
+          }
+          double S[Cfg::GSTATE ? CH : 1];
+          if constexpr (Cfg::GSTATE) {
+            if (!first) {
+#pragma unroll
+              for (int j = 0; j < CH; ++j) S[j] = __ldcg(gst + (int64_t)(c0 + j) * kBM);
             }
           }
           tmem_wait_ld();
@@ -278,6 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               acc = 0.0;
               if (g.beta != 0.0 && rvalid && col0 + c0 + j < g.M)
                 acc = g.beta * g.Cin[row * g.ldcin + col0 + c0 + j];
+            } else if constexpr (Cfg::GSTATE) {
+              acc = S[j];
             } else {
               acc = __hiloint2double((int)H[j], (int)L[j]);
             }
@@ -287,24 +363,23 @@ __global__ void __launch_bounds__(kThreads, 1)
               acc = fma(pj, g.alpha * __longlong_as_double((long long)(ea + eb + 1023) << 52), acc);
             else  // outside the normal range: scale in two exact steps
               acc = fma(pj * pow2d(ea), g.alpha * pow2d(eb), acc);
-            if (last) {
-              L[j] = (uint32_t)__double2loint(acc);
-              H[j] = (uint32_t)__double2hiint(acc);
-              if (rvalid && col0 + c0 + j < g.M) {
-                const int64_t col = col0 + c0 + j;
-                if (!g.symmetric) {
-                  g.C[row * g.ldc + col] = acc;
-                } else if (tm != tn || col >= row) {
-                  g.C[row * g.ldc + col] = acc;
-                  g.C[col * g.ldc + row] = acc;
-                }
-              }
+            if constexpr (Cfg::GSTATE) {
+              if (!last) __stcg(gst + (int64_t)(c0 + j) * kBM, acc);
             } else {
               L[j] = (uint32_t)__double2loint(acc);
               H[j] = (uint32_t)__double2hiint(acc);
             }
+            if (last && rvalid && col0 + c0 + j < g.M) {
+              const int64_t col = col0 + c0 + j;
+              if (!g.symmetric) {
+                g.C[row * g.ldc + col] = acc;
+              } else if (tm != tn || col >= row) {
+                g.C[row * g.ldc + col] = acc;
+                g.C[col * g.ldc + row] = acc;
+              }
+            }
           }
-          if (!last) {
+          if (!Cfg::GSTATE && !last) {
             if constexpr (CH == 32) {
               tmem_st32(t_lo + c0, L);
               tmem_st32(t_hi + c0, H);
@@ -317,22 +392,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acce[buf]);
+        if (lane == 0) {
+          if constexpr (PAIR) mbar_arrive_cluster(acce_leader + buf * sizeof(uint64_t));
+          else mbar_arrive(&acce[buf]);
+        }
         ++acc_it;
       }
     }
   }
 
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the pair finishes together before TMEM is freed
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+    else tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
 }
 
 // ---------------------------------------------------------------- host side
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+// Diagnostics: with OZK_GEMM_STATS=1 each launch records, per CTA, the cycles
+// its MMA thread waited for a free accumulator and for loaded stages, the
+// cycles its producer waited for free stages, and the MMA thread's total;
+// ozk_gemm_stats() returns the sums of the last launch.
+static unsigned long long* g_stats_dev[64] = {nullptr};
+static int g_stats_ctas[64] = {0};
+static int g_stats_last_dev = -1;
+
+static bool stats_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("OZK_GEMM_STATS");
+    v = (s && s[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// CTA-pair tiles are the default for wide outputs; OZK_GEMM_PAIR=0 selects
+// single-CTA tiles (kept for comparison and as a fallback).
+static bool pair_mode_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("OZK_GEMM_PAIR");
+    v = (s && s[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
 
 static int get_encode_fn() {
   if (g_encode) return OZK_OK;
@@ -361,31 +469,56 @@ static int make_slice_map(CUtensorMap* map, const uint16_t* base, int64_t k_pad,
   return OZK_OK;
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 static int launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const PairList& pl,
                      const GemmArgs& ga, int dev, cudaStream_t stream) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, PAIR>;
   static int configured[64] = {0};
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_slice_gemm<BN>,
+    cudaError_t e = cudaFuncSetAttribute(k_slice_gemm<BN, PAIR>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k_slice_gemm)", e);
     configured[dev] = 1;
   }
-  int sms = device_sm_count(dev);
-  int grid = ga.num_tiles < sms ? ga.num_tiles : sms;
-  k_slice_gemm<BN><<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(ma, mb, pl, ga);
-  cudaError_t e = cudaGetLastError();
+  const int sms = device_sm_count(dev);
+  const int per = PAIR ? 2 : 1;
+  const int max_units = sms / per;
+  const int units = ga.num_tiles < max_units ? ga.num_tiles : max_units;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(units * per));
+  cfg.blockDim = dim3(Cfg::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = per;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  GemmArgs gl = ga;
+  if (stats_enabled()) {
+    if (!g_stats_dev[dev]) cudaMalloc(&g_stats_dev[dev], 4 * 1024 * sizeof(unsigned long long));
+    cudaMemsetAsync(g_stats_dev[dev], 0, 4 * 1024 * sizeof(unsigned long long), stream);
+    gl.stats = g_stats_dev[dev];
+    g_stats_ctas[dev] = units * per;
+    g_stats_last_dev = dev;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_slice_gemm<BN, PAIR>, ma, mb, pl, gl);
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_slice_gemm launch", e);
+}
+
+size_t gemm_state_bytes(int dev) {
+  return (size_t)device_sm_count(dev) * GemmCfg<256, true>::STATE_PER_CTA * sizeof(double);
 }
 
 int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t* SB,
                       const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
                       const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
                       int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
-                      double* C, int64_t ldc, float* products, int32_t* status,
-                      cudaStream_t stream) {
+                      double* C, int64_t ldc, float* products, double* state, size_t state_bytes,
+                      int32_t* status, cudaStream_t stream) {
   if (N == 0 || M == 0) return OZK_OK;
   if (n_pairs < 1 || n_pairs > OZK_MAX_PAIRS) return set_error(OZK_ERR_ARG, "n_pairs out of range");
   if (k_pad <= 0 || k_pad % OZK_KB) return set_error(OZK_ERR_ARG, "k_pad must be a positive multiple of 64");
@@ -405,12 +538,19 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
   int dev;
   cudaGetDevice(&dev);
 
-  // Narrow outputs (e.g. residual right-hand sides) use a narrow tile.
-  const int BN = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
-  const int bn = symmetric ? 128 : BN;
+  // Tile choice: 256 x 256 on CTA pairs (FP64 sums in the per-CTA state
+  // scratch) for large FP64 outputs; 256 x 128 on CTA pairs (sums in TMEM)
+  // when no scratch is given; narrow single-CTA tiles for narrow outputs
+  // (e.g. residual right-hand sides).
+  const bool wide = mode == OZK_ACC_F64 && N >= 256 && M >= 256 && state &&
+                    state_bytes >= gemm_state_bytes(dev) && pair_mode_enabled();
+  const int BN = wide ? 256 : (M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128)));
+  const int bn = (symmetric && !wide) ? 128 : BN;
+  const bool pair = wide || (!symmetric && bn == 128 && pair_mode_enabled());
+  const int tile_m = pair ? 2 * kBM : kBM;
   CUtensorMap ma, mb;
   if ((rc = make_slice_map(&ma, SA, k_pad, N, nA, kBM))) return rc;
-  if ((rc = make_slice_map(&mb, SB, k_pad, M, nB, bn))) return rc;
+  if ((rc = make_slice_map(&mb, SB, k_pad, M, nB, pair ? bn / 2 : bn))) return rc;
 
   PairList pl;
   memset(&pl, 0, sizeof(pl));
@@ -427,7 +567,7 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
   ga.M = M;
   ga.num_kb = (int)(k_pad / OZK_KB);
   ga.nB = nB;
-  ga.tiles_m = (int)((N + kBM - 1) / kBM);
+  ga.tiles_m = (int)((N + tile_m - 1) / tile_m);
   ga.tiles_n = (int)((M + bn - 1) / bn);
   ga.num_tiles = symmetric ? ga.tiles_m * (ga.tiles_m + 1) / 2 : ga.tiles_m * ga.tiles_n;
   ga.group_m = 8;
@@ -442,12 +582,30 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
   ga.products = products;
   ga.status = status;
   ga.budget_ns = wait_budget_ns();
+  ga.state = state;
+  if (wide) return launch_bn<256, true>(ma, mb, pl, ga, dev, stream);
   switch (bn) {
-    case 16: return launch_bn<16>(ma, mb, pl, ga, dev, stream);
-    case 32: return launch_bn<32>(ma, mb, pl, ga, dev, stream);
-    case 64: return launch_bn<64>(ma, mb, pl, ga, dev, stream);
-    default: return launch_bn<128>(ma, mb, pl, ga, dev, stream);
+    case 16: return launch_bn<16, false>(ma, mb, pl, ga, dev, stream);
+    case 32: return launch_bn<32, false>(ma, mb, pl, ga, dev, stream);
+    case 64: return launch_bn<64, false>(ma, mb, pl, ga, dev, stream);
+    default:
+      return pair ? launch_bn<128, true>(ma, mb, pl, ga, dev, stream)
+                  : launch_bn<128, false>(ma, mb, pl, ga, dev, stream);
   }
 }
 
 }  // namespace ozk
+
+extern "C" int ozk_gemm_stats(unsigned long long* out4) {
+  using namespace ozk;
+  if (!out4) return OZK_ERR_ARG;
+  for (int i = 0; i < 4; ++i) out4[i] = 0;
+  const int dev = g_stats_last_dev;
+  if (dev < 0 || !g_stats_dev[dev]) return OZK_ERR_UNSUPPORTED;
+  unsigned long long h[4 * 1024];
+  cudaDeviceSynchronize();
+  cudaMemcpy(h, g_stats_dev[dev], sizeof(h), cudaMemcpyDeviceToHost);
+  for (int c = 0; c < g_stats_ctas[dev] && c < 1024; ++c)
+    for (int i = 0; i < 4; ++i) out4[i] += h[4 * c + i];
+  return g_stats_ctas[dev];
+}

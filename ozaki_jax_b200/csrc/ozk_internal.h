@@ -42,8 +42,13 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
                       const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
                       const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
                       int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
-                      double* C, int64_t ldc, float* products, int32_t* status,
-                      cudaStream_t stream);
+                      double* C, int64_t ldc, float* products, double* state, size_t state_bytes,
+                      int32_t* status, cudaStream_t stream);
+// Bytes of the per-CTA FP64 state scratch the 256-wide GEMM tiles need.
+size_t gemm_state_bytes(int dev);
+// Smallest workspace ozk_matmul_f64 (OZK_ACC_F64) accepts: without the state
+// scratch it runs 128-wide tiles.
+size_t matmul_min_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo);
 int launch_accumulate_2sum(const float* products, const int32_t* eA, const int32_t* eB, int64_t N,
                            int64_t M, int n_hi, int n_lo, float* C_hi, float* C_lo, double* C,
                            int64_t ldc, cudaStream_t stream);

@@ -59,7 +59,7 @@ extern "C" int ozk_matmul_f64_noalloc(const double* A, int64_t lda, const double
   if (n_hi < 1 || n_lo < 0 || n_hi > OZK_MAX_SIDE || n_lo > OZK_MAX_SIDE)
     return ozk::set_error(OZK_ERR_ARG, "n_hi must be in [1,%d] and n_lo in [0,%d]", OZK_MAX_SIDE,
                           OZK_MAX_SIDE);
-  const size_t need = ozk_matmul_workspace_bytes(N, K, M, n_hi, n_lo);
+  const size_t need = ozk::matmul_min_workspace_bytes(N, K, M, n_hi, n_lo);
   if (need > (size_t)OZK_NOALLOC_SCRATCH_BYTES)
     return ozk::set_error(OZK_ERR_WORKSPACE,
                           "ozk_matmul_f64_noalloc: %lld x %lld x %lld with %d+%d slices needs %zu "

@@ -36,10 +36,16 @@ def extract_device(X, rho, n_hi, n_lo, axis):
     slices = torch.empty((ns, lines, k_pad), dtype=torch.int16, device=dev)
     exps = torch.empty((ns, lines), dtype=torch.int32, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    fn = lib.ozk_extract_rows_f64 if axis == 1 else lib.ozk_extract_cols_f64
-    args = (X.data_ptr(), X.stride(0)) + ((lines, K) if axis == 1 else (K, lines))
-    L.check(fn(*args, rho, n_hi, n_lo, slices.data_ptr(), k_pad, exps.data_ptr(),
-               status.data_ptr(), D.stream_handle(dev)))
+    if axis == 1:
+        L.check(lib.ozk_extract_rows_f64(X.data_ptr(), X.stride(0), lines, K, rho, n_hi, n_lo,
+                                         slices.data_ptr(), k_pad, exps.data_ptr(),
+                                         status.data_ptr(), D.stream_handle(dev)))
+    else:
+        scratch = torch.empty(lines * K, dtype=torch.float64, device=dev)
+        L.check(lib.ozk_extract_cols_f64(X.data_ptr(), X.stride(0), K, lines, rho, n_hi, n_lo,
+                                         slices.data_ptr(), k_pad, exps.data_ptr(),
+                                         scratch.data_ptr(), scratch.numel() * 8,
+                                         status.data_ptr(), D.stream_handle(dev)))
     return slices, k_pad, exps, status
 
 

@@ -46,7 +46,7 @@ def run_products(SA, SB, eA, eB, k_pad, n_hi, n_lo):
     st = torch.zeros(1, dtype=torch.int32, device="cuda")
     rc = L.load().ozk_slice_gemm(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(), eB.data_ptr(),
                                  nS, N, M, k_pad, pa, pb, n, L.OZK_ACC_PRODUCTS, 0, 1.0, 0.0,
-                                 None, 0, None, 0, P.data_ptr(), st.data_ptr(),
+                                 None, 0, None, 0, P.data_ptr(), None, 0, st.data_ptr(),
                                  torch.cuda.current_stream().cuda_stream)
     L.check(rc)
     torch.cuda.synchronize()
@@ -86,7 +86,7 @@ def test_products_exact_at_the_bound():
     P = torch.empty((1, N, M), dtype=torch.float32, device="cuda")
     L.check(L.load().ozk_slice_gemm(SA.data_ptr(), e.data_ptr(), 1, SB.data_ptr(), e.data_ptr(), 1,
                                     N, M, K, pa, pb, 1, L.OZK_ACC_PRODUCTS, 0, 1.0, 0.0, None, 0,
-                                    None, 0, P.data_ptr(), None,
+                                    None, 0, P.data_ptr(), None, 0, None,
                                     torch.cuda.current_stream().cuda_stream))
     exact = sa[0].astype(np.float64) @ sb[0].astype(np.float64).T
     got = P.cpu().numpy()[0].astype(np.float64)

@@ -197,9 +197,12 @@ def ours(args):
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     pa = (ctypes.c_uint8 * 256)()
     pb = (ctypes.c_uint8 * 256)()
-    npairs = lib.ozk_pair_schedule(n_hi, n_lo, pa, pb, 256)
+    # the pipeline's order for accumulation='fused' (order-independent sums)
+    npairs = lib.ozk_pair_schedule_snake(n_hi, n_lo, pa, pb, 256)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
+
+    ACC = _lib.OZK_ACC_FIXED  # accumulation='fused
 
     def step(evs=None):
         if evs:
@@ -215,8 +218,8 @@ def ours(args):
             evs[1].record(stream)
         _lib.check(lib.ozk_slice_gemm(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(),
                                       eB.data_ptr(), nS, nb, m, k_pad, pa, pb, npairs,
-                                      _lib.OZK_ACC_F64, 0, 1.0, 0.0, None, 0, C.data_ptr(), m,
-                                      None, GW.data_ptr(), GW.numel(), status.data_ptr(), sh))
+                                      ACC, 0, 1.0, 0.0, None, 0, C.data_ptr(), m,
+                                      None, GW.data_ptr(), GW.numel(), rho, status.data_ptr(), sh))
         if evs:
             evs[2].record(stream)
 
@@ -251,12 +254,14 @@ def ours(args):
         total_ms, gemm_ms, extract_ms = t.tolist()
     gemm_waits = None
     if os.environ.get("OZK_GEMM_STATS") == "1":
-        w = (ctypes.c_ulonglong * 4)()
+        w = (ctypes.c_ulonglong * 8)()
         n_ctas = lib.ozk_gemm_stats(w)
         if n_ctas > 0 and w[3]:
             gemm_waits = {"mma_wait_accumulator": w[0] / w[3], "mma_wait_loads": w[1] / w[3],
                           "producer_wait_free_stage_cycles_per_cta": w[2] / n_ctas,
-                          "mma_total_cycles_per_cta": w[3] / n_ctas}
+                          "mma_total_cycles_per_cta": w[3] / n_ctas,
+                          "epilogue_wait_cycles_per_pair": w[4] / max(w[6], 1),
+                          "epilogue_busy_cycles_per_pair": w[5] / max(w[6], 1)}
     ms_step = total_ms / args.steps
     flops_fp64eq = 2.0 * n * k * m
     value = flops_fp64eq / (ms_step * 1e-3) / 1e12

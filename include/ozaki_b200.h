@@ -52,6 +52,7 @@ typedef enum {
 /* Accumulation modes of ozk_slice_gemm. */
 #define OZK_ACC_F64 0       /* FP64 running sum in the GEMM epilogue -> C (double) */
 #define OZK_ACC_PRODUCTS 1  /* write each pair's exact FP32 product -> products */
+#define OZK_ACC_FIXED 2     /* exact int64 fixed-point sum (on-device slices) -> C */
 
 /* ---------------------------------------------------------------- policies */
 
@@ -63,6 +64,9 @@ int ozk_compute_rho_f64(int64_t K);
  * slice-pair order (hi x hi, hi x lo, lo x hi) into pair_a/pair_b (capacity
  * `cap`) and returns the pair count, or OZK_ERR_ARG. */
 int ozk_pair_schedule(int n_hi, int n_lo, uint8_t* pair_a, uint8_t* pair_b, int cap);
+/* The same pairs in an L2-friendly order (consecutive pairs share an operand
+ * slice), used with order-independent OZK_ACC_FIXED sums. */
+int ozk_pair_schedule_snake(int n_hi, int n_lo, uint8_t* pair_a, uint8_t* pair_b, int cap);
 /* Host-pipeline triangular schedule i + j <= n-1 (ozaki_jax/matmul.py:23-32). */
 int ozk_triangular_schedule(int n_slices, uint8_t* pair_a, uint8_t* pair_b, int cap);
 
@@ -109,6 +113,10 @@ int ozk_extract_cols_host_f64(const double* X, int64_t ldx, int64_t K, int64_t c
  * mode OZK_ACC_F64:  C[r][c] = beta*Cin[r][c] + alpha * sum_p P_p[r][c]
  *                    * 2^(eA[a][r] + eB[b][c]), summed in FP64 in pair order
  *                    (Cin may be NULL when beta == 0).
+ * mode OZK_ACC_FIXED: the same sum computed exactly in an int64 per element whose
+ *                    unit is 2^(2(rho-24) - 36 + eA[0][r] + eB[0][c]) (slice 0 must be
+ *                    the top slice on both sides, rho the extraction's), rounded
+ *                    to FP64 once: accuracy of an FP64 sum without FP64 work per pair.
  * mode OZK_ACC_PRODUCTS: products[p][r][c] = P_p[r][c] (FP32, exact), ld = M.
  * symmetric != 0 (gram): requires SA == SB, eA == eB, N == M; only tiles on
  * or above the diagonal are computed and each is also written mirrored, so C
@@ -120,7 +128,7 @@ int ozk_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t
                    const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
                    int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
                    double* C, int64_t ldc, float* products, void* workspace, size_t ws_bytes,
-                   int32_t* status_dev, void* stream);
+                   int rho, int32_t* status_dev, void* stream);
 /* Scratch ozk_slice_gemm uses for its 256-wide tiles (per-CTA FP64 running
  * sums, L2-resident); with a smaller or NULL workspace it runs 128-wide tiles
  * that keep the sums in TMEM. */
@@ -148,14 +156,17 @@ size_t ozk_matmul_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int
  * ozaki_jax/matmul.py:514-540, :641-686): C = A @ B with FP64 inputs and
  * output on the device.  rho < 0 selects _compute_rho_f32(K).  workspace may be
  * NULL (then it is taken from the stream-ordered pool and returned).
- * acc_mode: OZK_ACC_F64 (FP64 epilogue) or OZK_ACC_PRODUCTS (materialised
- * products + reference 2Sum, bit-identical to the reference's result). */
+ * acc_mode: OZK_ACC_FIXED (exact int64 fixed-point sums, rounded to FP64 once:
+ * the 'fused' / 'bf16_interleaved' default), OZK_ACC_F64 (FP64 sums in pair
+ * order: the reference's FP64 'host' accumulation) or OZK_ACC_PRODUCTS
+ * (materialised products + the reference's FP32 2Sum, bit-identical to the
+ * reference's 'ondevice' / 'fused' result). */
 int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
                    int64_t ldc, int64_t N, int64_t K, int64_t M, int rho, int n_hi, int n_lo,
                    int acc_mode, void* workspace, size_t ws_bytes, int32_t* status_dev,
                    void* stream);
 
-/* Allocation-free variant of ozk_matmul_f64 (acc_mode OZK_ACC_F64, rho from K).
+/* Allocation-free variant of ozk_matmul_f64 (acc_mode OZK_ACC_FIXED, rho from K).
  * It has no counterpart in the reference.  For callers that must not allocate
  * device memory during a call (a process whose framework owns the GPU's memory,
  * such as JAX/XLA reserving most of it for its own allocator, or a plugin
@@ -208,10 +219,13 @@ const char* ozk_strerror(int status);
 int ozk_last_error_detail(char* buf, size_t len);
 /* Diagnostics (no counterpart in the reference): with OZK_GEMM_STATS=1 in
  * the environment, sums over the CTAs of the last slice-GEMM launch of
- * {MMA-thread cycles waiting for a free accumulator, MMA-thread cycles waiting
- * for loaded stages, producer cycles waiting for free stages, MMA-thread total
- * cycles}; returns the CTA count (synchronises the device). */
-int ozk_gemm_stats(unsigned long long* out4);
+ * {0: MMA-thread cycles waiting for a free accumulator, 1: MMA-thread cycles
+ * waiting for loaded stages, 2: producer cycles waiting for free stages,
+ * 3: MMA-thread total cycles, 4: epilogue cycles waiting for a finished
+ * accumulator, 5: epilogue cycles processing, 6: epilogue pairs, 7: 0}
+ * (epilogue figures from one warp per CTA); returns the CTA count
+ * (synchronises the device). */
+int ozk_gemm_stats(unsigned long long* out8);
 /* Library version string. */
 const char* ozk_version(void);
 

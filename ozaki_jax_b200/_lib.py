@@ -25,6 +25,7 @@ OZK_FLAG_RANGE = 0x4
 
 OZK_ACC_F64 = 0
 OZK_ACC_PRODUCTS = 1
+OZK_ACC_FIXED = 2
 
 c_i64 = ctypes.c_int64
 c_int = ctypes.c_int
@@ -37,6 +38,7 @@ SIGNATURES = {
     "ozk_compute_rho_f32": (c_int, [c_i64]),
     "ozk_compute_rho_f64": (c_int, [c_i64]),
     "ozk_pair_schedule": (c_int, [c_int, c_int, vp, vp, c_int]),
+    "ozk_pair_schedule_snake": (c_int, [c_int, c_int, vp, vp, c_int]),
     "ozk_triangular_schedule": (c_int, [c_int, vp, vp, c_int]),
     "ozk_extract_rows_f64": (c_int, [vp, c_i64, c_i64, c_i64, c_int, c_int, c_int, vp, c_i64, vp,
                                      vp, vp]),
@@ -48,7 +50,7 @@ SIGNATURES = {
                                           vp, vp]),
     "ozk_slice_gemm": (c_int, [vp, vp, c_int, vp, vp, c_int, c_i64, c_i64, c_i64, vp, vp, c_int,
                                c_int, c_int, c_dbl, c_dbl, vp, c_i64, vp, c_i64, vp, vp, c_size,
-                               vp, vp]),
+                               c_int, vp, vp]),
     "ozk_slice_gemm_workspace_bytes": (c_size, []),
     "ozk_accumulate_2sum": (c_int, [vp, vp, vp, c_i64, c_i64, c_int, c_int, vp, vp, vp, c_i64,
                                     vp]),

@@ -96,6 +96,36 @@ static int ondevice_pairs(int n_hi, int n_lo, uint8_t* pa, uint8_t* pb, int cap)
   return n;
 }
 
+// Pair order for order-independent (fixed-point) sums: the same pairs as
+// ondevice_pairs, arranged so consecutive pairs share an operand slice (the
+// hi x hi block row by row in alternating direction, then hi x lo walking back
+// over the A slices, then lo x hi), which keeps one operand panel hot in L2
+// at every pair boundary.
+static int snake_pairs(int n_hi, int n_lo, uint8_t* pa, uint8_t* pb, int cap) {
+  int n = ondevice_pairs(n_hi, n_lo, pa, pb, cap);
+  if (n < 0) return n;
+  int k = 0;
+  int last_i = 0;
+  for (int i = 0; i < n_hi; ++i) {
+    for (int jj = 0; jj < n_hi; ++jj) {
+      const int j = (i % 2 == 0) ? jj : n_hi - 1 - jj;
+      pa[k] = (uint8_t)i, pb[k++] = (uint8_t)j;
+    }
+    last_i = i;
+  }
+  for (int j = 0; j < n_lo; ++j)
+    for (int ii = 0; ii < n_hi; ++ii) {
+      const int i = ((j % 2 == 0) == (last_i == n_hi - 1)) ? n_hi - 1 - ii : ii;
+      pa[k] = (uint8_t)i, pb[k++] = (uint8_t)(n_hi + j);
+    }
+  for (int i = 0; i < n_lo; ++i)
+    for (int jj = 0; jj < n_hi; ++jj) {
+      const int j = (i % 2 == 0) ? jj : n_hi - 1 - jj;
+      pa[k] = (uint8_t)(n_hi + i), pb[k++] = (uint8_t)j;
+    }
+  return k == n ? n : set_error(OZK_ERR_ARG, "pair schedule mismatch");
+}
+
 struct Workspace {
   uint16_t* SA;
   uint16_t* SB;
@@ -198,6 +228,11 @@ int ozk_pair_schedule(int n_hi, int n_lo, uint8_t* pair_a, uint8_t* pair_b, int 
   return ondevice_pairs(n_hi, n_lo, pair_a, pair_b, cap);
 }
 
+int ozk_pair_schedule_snake(int n_hi, int n_lo, uint8_t* pair_a, uint8_t* pair_b, int cap) {
+  if (!pair_a || !pair_b) return set_error(OZK_ERR_ARG, "NULL pair arrays");
+  return snake_pairs(n_hi, n_lo, pair_a, pair_b, cap);
+}
+
 int ozk_triangular_schedule(int n_slices, uint8_t* pair_a, uint8_t* pair_b, int cap) {
   if (!pair_a || !pair_b || n_slices < 1 || n_slices > OZK_MAX_SLICES)
     return set_error(OZK_ERR_ARG, "n_slices out of range");
@@ -282,17 +317,17 @@ int ozk_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t
                    const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
                    int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
                    double* C, int64_t ldc, float* products, void* workspace, size_t ws_bytes,
-                   int32_t* status_dev, void* stream) {
+                   int rho, int32_t* status_dev, void* stream) {
   if (!SA || !SB || !eA || !eB || !pair_a || !pair_b) return set_error(OZK_ERR_ARG, "NULL pointer");
   if (N < 0 || M < 0) return set_error(OZK_ERR_ARG, "bad shape");
-  if (mode == OZK_ACC_F64 && ldc < M) return set_error(OZK_ERR_ARG, "ldc < M");
+  if (mode != OZK_ACC_PRODUCTS && ldc < M) return set_error(OZK_ERR_ARG, "ldc < M");
   if (beta != 0.0 && ldcin < M) return set_error(OZK_ERR_ARG, "ldcin < M");
   if (alpha != 1.0 && alpha != -1.0) return set_error(OZK_ERR_ARG, "alpha must be +1 or -1");
   if (workspace && ((uintptr_t)workspace & 255))
     return set_error(OZK_ERR_ARG, "workspace not 256-byte aligned");
   return launch_slice_gemm(SA, eA, nA, SB, eB, nB, N, M, k_pad, pair_a, pair_b, n_pairs, mode,
                            symmetric, alpha, beta, Cin, ldcin, C, ldc, products, (double*)workspace,
-                           workspace ? ws_bytes : 0, status_dev, (cudaStream_t)stream);
+                           workspace ? ws_bytes : 0, rho, status_dev, (cudaStream_t)stream);
 }
 
 size_t ozk_slice_gemm_workspace_bytes(void) { return cur_state_bytes(); }
@@ -325,10 +360,11 @@ int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, d
   if (!A || !B || !C) return set_error(OZK_ERR_ARG, "NULL pointer");
   if (N < 0 || M < 0 || K < 1) return set_error(OZK_ERR_ARG, "bad shape (K must be >= 1)");
   if (lda < K || ldb < M || ldc < M) return set_error(OZK_ERR_ARG, "leading dimension too small");
-  if (acc_mode != OZK_ACC_F64 && acc_mode != OZK_ACC_PRODUCTS)
+  if (acc_mode != OZK_ACC_F64 && acc_mode != OZK_ACC_PRODUCTS && acc_mode != OZK_ACC_FIXED)
     return set_error(OZK_ERR_ARG, "bad acc_mode");
   uint8_t pa[OZK_MAX_PAIRS], pb[OZK_MAX_PAIRS];
-  int np = ondevice_pairs(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS);
+  int np = acc_mode == OZK_ACC_FIXED ? snake_pairs(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS)
+                                     : ondevice_pairs(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS);
   if (np < 0) return np;
   if (rho < 0) rho = rho_f32(K);
   int rc = check_bound(K, 24 - rho);
@@ -355,12 +391,12 @@ int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, d
                                 s)))
     return rc;
   if (!prod)
-    return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np, OZK_ACC_F64,
-                             0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, w.state, w.state_bytes,
+    return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np, acc_mode, 0,
+                             1.0, 0.0, nullptr, 0, C, ldc, nullptr, w.state, w.state_bytes, rho,
                              status_dev, s);
   if ((rc = launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np,
                               OZK_ACC_PRODUCTS, 0, 1.0, 0.0, nullptr, 0, nullptr, 0, w.products,
-                              nullptr, 0, status_dev, s)))
+                              nullptr, 0, rho, status_dev, s)))
     return rc;
   return launch_accumulate_2sum(w.products, w.eA, w.eB, N, M, n_hi, n_lo, nullptr, nullptr, C, ldc,
                                 s);
@@ -405,7 +441,7 @@ int ozk_matmul_host_f64(const double* A, int64_t lda, const double* B, int64_t l
     return rc;
   return launch_slice_gemm(w.SA, w.eA, n_slices, w.SB, w.eB, n_slices, N, M, k_pad, pa, pb, np,
                            OZK_ACC_F64, 0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, w.state,
-                           w.state_bytes, status_dev, s);
+                           w.state_bytes, rho, status_dev, s);
 }
 
 // gram: the column extraction of A (N x K) gives, per column of A, slices over
@@ -422,7 +458,7 @@ int ozk_gram_f64(const double* A, int64_t lda, double* G, int64_t ldg, int64_t N
   if (N < 1 || K < 0) return set_error(OZK_ERR_ARG, "bad shape (N must be >= 1)");
   if (lda < K || ldg < K) return set_error(OZK_ERR_ARG, "leading dimension too small");
   uint8_t pa[OZK_MAX_PAIRS], pb[OZK_MAX_PAIRS];
-  int np = ondevice_pairs(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS);
+  int np = snake_pairs(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS);
   if (np < 0) return np;
   if (rho < 0) rho = rho_f32(N);
   int rc = check_bound(N, 24 - rho);
@@ -443,8 +479,8 @@ int ozk_gram_f64(const double* A, int64_t lda, double* G, int64_t ldg, int64_t N
   if ((rc = launch_extract_cols(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, w.BT,
                                 s)))
     return rc;
-  return launch_slice_gemm(w.SA, w.eA, nS, w.SA, w.eA, nS, K, K, k_pad, pa, pb, np, OZK_ACC_F64, 1,
-                           1.0, 0.0, nullptr, 0, G, ldg, nullptr, w.state, w.state_bytes,
+  return launch_slice_gemm(w.SA, w.eA, nS, w.SA, w.eA, nS, K, K, k_pad, pa, pb, np, OZK_ACC_FIXED,
+                           1, 1.0, 0.0, nullptr, 0, G, ldg, nullptr, w.state, w.state_bytes, rho,
                            status_dev, s);
 }
 
@@ -461,7 +497,7 @@ int ozk_residual_f64(const double* A, int64_t lda, const double* X, int64_t ldx,
   if (lda < K || ldx < M || ldb < M || ldr < M)
     return set_error(OZK_ERR_ARG, "leading dimension too small");
   uint8_t pa[OZK_MAX_PAIRS], pb[OZK_MAX_PAIRS];
-  int np = ondevice_pairs(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS);
+  int np = snake_pairs(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS);
   if (np < 0) return np;
   if (rho < 0) rho = rho_f32(K);
   int rc = check_bound(K, 24 - rho);
@@ -484,9 +520,9 @@ int ozk_residual_f64(const double* A, int64_t lda, const double* X, int64_t ldx,
   if ((rc = launch_extract_cols(X, ldx, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, w.BT,
                                 s)))
     return rc;
-  return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np, OZK_ACC_F64, 0,
-                           -1.0, 1.0, Bv, ldb, R, ldr, nullptr, w.state, w.state_bytes, status_dev,
-                           s);
+  return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np, OZK_ACC_FIXED,
+                           0, -1.0, 1.0, Bv, ldb, R, ldr, nullptr, w.state, w.state_bytes, rho,
+                           status_dev, s);
 }
 
 int ozk_check_status(const int32_t* status_dev, void* stream) {

@@ -147,6 +147,20 @@ __device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const CUtensorM
       : "memory");
 }
 
+// Prefetch a 3D tile into L2 (no shared-memory destination, no completion).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   (uint64_t)map),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+// 32-byte vector store (sm_100): p must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v4_f64(double* p, double a, double b, double c, double d) {
+  asm volatile("st.global.v4.f64 [%0], {%1, %2, %3, %4};" ::"l"(p), "d"(a), "d"(b), "d"(c), "d"(d)
+               : "memory");
+}
+
 // shared::cluster address of the object at local address `p` in CTA `rank`.
 __device__ __forceinline__ uint32_t mapa_u32(const void* p, uint32_t rank) {
   uint32_t r;

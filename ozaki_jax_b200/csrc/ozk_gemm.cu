@@ -63,6 +63,11 @@ struct GemmArgs {
   uint64_t budget_ns;
   unsigned long long* stats;  // optional per-CTA wait-cycle counters (diagnostics)
   double* state;              // per-CTA FP64 running sums (BN = 256 tiles)
+  int c_vec;                  // C is 32-byte aligned with ldc % 4 == 0
+  int fixed;                  // 1: int64 fixed-point sums (OZK_ACC_FIXED), 0: FP64 sums
+  int fix_off;                // -150 - G + kFixFrac, G = product-grid exponent 2 (rho - 24)
+  int fix_scale;              // G - kFixFrac: output = sum * 2^(eA0 + eB0 + fix_scale)
+  int prefetch;               // L2 prefetch distance in stages (0 = off)
 };
 
 // PAIR = false: one CTA per output tile of 128 x BN.
@@ -112,6 +117,54 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& tm, i
   int r = t - grp * per_group;
   tm = first + r % gsz;
   tn = r / gsz;
+}
+
+// Fixed-point accumulation.  With the top slices' exponents eA0 (row) and
+// eB0 (column), every exact slice product P of a pair is an integer number
+// of product-grid units g = 2^G (G = 2 (rho - 24)) with |P/g| < 2^26 (the
+// preflight bound); scaled by 2^(ea + eb - eA0 - eB0) <= 1 it is summed
+// exactly in an int64 whose unit is g * 2^(eA0 + eB0 - kFixFrac).  Terms are
+// < 2^62 and only parts below the unit (2^-36 of the top grid) are rounded
+// away, so the sum is as accurate as FP64 accumulation and independent of the
+// order -- and the per-pair work uses only the integer pipes (FP64 arithmetic
+// shares a pipe with the tensor cores on this part).
+constexpr int kFixFrac = 36;
+
+// Term of the FP32 product bits u, t_off = (ea - eA0) + (eb - eB0) + fix_off:
+// round(P * 2^(ea + eb) / unit).
+__device__ __forceinline__ long long fixed_term(uint32_t u, int t_off) {
+  const uint32_t ex = (u >> 23) & 0xFFu;
+  const uint32_t m = (u & 0x7FFFFFu) | (ex ? 0x800000u : 0u);  // products are 0 or normal
+  const int T = (int)ex + t_off;
+  const int L = min(max(T, 0), 40);
+  const int R = min(max(-T, 0), 31);
+  const uint32_t mr = (m + ((1u << R) >> 1)) >> R;  // round half up
+  const long long v = (long long)((unsigned long long)mr << L);
+  const long long sg = (long long)((int)u >> 31);  // 0 or -1
+  return (v ^ sg) - sg;
+}
+
+// FP64 value of P * 2^e for the FP32 product bits u (exact), built with
+// integer operations only: the FP32 exponent field moves to the FP64 one with
+// e added, the mantissa shifts by 29.  Falls back to FP64 multiplies when the
+// result would leave the normal FP64 range.  sign_flip = 0x80000000 negates.
+__device__ __forceinline__ double scaled_term(uint32_t u, int e, uint32_t sign_flip) {
+  const uint32_t ex = (u >> 23) & 0xFFu;
+  if (ex == 0) return 0.0;  // products are 0 or normal
+  const int E = (int)ex + e + (1023 - 127);
+  if (E >= 1 && E <= 2046) {
+    const uint32_t hi = ((u & 0x80000000u) ^ sign_flip) | ((uint32_t)E << 20) | ((u >> 3) & 0xFFFFFu);
+    return __hiloint2double((int)hi, (int)(u << 29));
+  }
+  const double v = (double)__uint_as_float(u ^ sign_flip);
+  return (v * pow2d(e / 2)) * pow2d(e - e / 2);
+}
+
+// The FP64 value of a fixed-point sum: acc * 2^e, exact scaling.
+__device__ __forceinline__ double fixed_value(long long acc, int e) {
+  const double v = __ll2double_rn(acc);
+  if (e >= -1022 && e <= 1023) return v * __longlong_as_double((long long)(e + 1023) << 52);
+  return (v * pow2d(e / 2)) * pow2d(e - e / 2);
 }
 
 template <int BN, bool PAIR>
@@ -181,6 +234,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
           const int a = pairs.a[p], b = pairs.b[p];
           for (int kb = 0; kb < g.num_kb; ++kb) {
             const uint32_t s = it % STAGES, ph = (it / STAGES) & 1;
+            if (g.prefetch) {
+              // Pull the stage `prefetch` steps ahead (same tile, possibly the
+              // next pair) into L2 so pair boundaries do not wait on DRAM.
+              int pk = kb + g.prefetch, pp = p;
+              if (pk >= g.num_kb) {
+                pk -= g.num_kb;
+                ++pp;
+              }
+              if (pp < npairs && pk < g.num_kb) {
+                tma_prefetch_3d(&mapA, pk * OZK_KB, arow, pairs.a[pp]);
+                tma_prefetch_3d(&mapB, pk * OZK_KB, brow, pairs.b[pp]);
+              }
+            }
             long long c0 = clock64();
             if (!mbar_wait(&empty[s], ph ^ 1, s_abort, g.status, g.budget_ns)) {
               ok = false;
@@ -201,7 +267,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
           }
         }
       }
-      if (g.stats) g.stats[4 * blockIdx.x + 2] = (unsigned long long)w_empty;
+      if (g.stats) g.stats[8 * blockIdx.x + 2] = (unsigned long long)w_empty;
       // Drain: every issued copy must land before shared memory is released.
       // (In a pair only the even CTA's full barriers count the bytes.)
       if (!PAIR || rank == 0) {
@@ -262,7 +328,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
       else umma_commit(mma_done);
       mbar_wait(mma_done, 0, nullptr, g.status, g.budget_ns);
       if (g.stats) {
-        unsigned long long* st = g.stats + 4 * blockIdx.x;
+        unsigned long long* st = g.stats + 8 * blockIdx.x;
         st[0] = (unsigned long long)w_acc;
         st[1] = (unsigned long long)w_full;
         st[3] = (unsigned long long)(clock64() - t_start);
@@ -284,6 +350,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
     const uint32_t acce_leader = PAIR ? mapa_u32(&acce[0], 0) : 0;
     uint32_t acc_it = 0;
     bool ok = true;
+    long long ep_wait = 0, ep_busy = 0, ep_pairs = 0;
     for (int t = unit; ok && t < g.num_tiles; t += n_units) {
       int tm, tn;
       tile_coords(g, t, tm, tn);
@@ -294,17 +361,24 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
         s_eB[e] = c < g.M ? g.eB[(int64_t)(e / BN) * g.M + c] : 0;
       }
       named_bar(1, NE);
+      if (g.fixed) {  // slices >= 1 hold eb - eB0 (read after the barrier below)
+        for (int e = etid + BN; e < g.nB * BN; e += NE) s_eB[e] -= s_eB[e % BN];
+        named_bar(1, NE);
+      }
       const int64_t row = (int64_t)tm * Cfg::TILE_M + rank * kBM + q * 32 + lane;
       const bool rvalid = row < g.N;
+      const int eA0 = rvalid ? g.eA[row] : 0;
       for (int p = 0; p < npairs; ++p) {
         const uint32_t buf = acc_it & 1, aph = (acc_it >> 1) & 1;
         int got = 1;
+        const long long e0 = clock64();
         if (lane == 0) got = mbar_wait(&accf[buf], aph, s_abort, g.status, g.budget_ns);
         got = __shfl_sync(0xffffffffu, got, 0);
         if (!got) {
           ok = false;
           break;
         }
+        const long long e1 = clock64();
         tc_fence_after();
         const int a = pairs.a[p], b = pairs.b[p];
         const int ea = rvalid ? g.eA[(int64_t)a * g.N + row] : 0;
@@ -317,13 +391,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
           uint32_t P[CH], L[CH], H[CH];
           if constexpr (CH == 32) {
             tmem_ld32(t_acc + c0, P);
-            if (!Cfg::GSTATE && g.mode == OZK_ACC_F64 && !first) {
+            if (!Cfg::GSTATE && g.mode != OZK_ACC_PRODUCTS && !first) {
               tmem_ld32(t_lo + c0, L);
               tmem_ld32(t_hi + c0, H);
             }
           } else {
             tmem_ld16(t_acc + c0, P);
-            if (!Cfg::GSTATE && g.mode == OZK_ACC_F64 && !first) {
+            if (!Cfg::GSTATE && g.mode != OZK_ACC_PRODUCTS && !first) {
               tmem_ld16(t_lo + c0, L);
               tmem_ld16(t_hi + c0, H);
             }
@@ -345,6 +419,45 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
             }
             continue;
           }
+          if (g.fixed) {
+            // ---- int64 fixed-point sums (integer pipes only until the last pair)
+            const int ta = ea - eA0 + g.fix_off;
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+              const int db = b == 0 ? 0 : s_eB[b * BN + c0 + j];  // eb - eB0
+              long long acc = fixed_term(P[j], ta + db);
+              if (!first) {
+                if constexpr (Cfg::GSTATE) acc += __double_as_longlong(S[j]);
+                else acc += (long long)(((unsigned long long)H[j] << 32) | L[j]);
+              }
+              if (!last) {
+                if constexpr (Cfg::GSTATE) {
+                  __stcg(gst + (int64_t)(c0 + j) * kBM, __longlong_as_double(acc));
+                } else {
+                  L[j] = (uint32_t)acc;
+                  H[j] = (uint32_t)((unsigned long long)acc >> 32);
+                }
+              } else {
+                double v = fixed_value(acc, eA0 + s_eB[c0 + j] + g.fix_scale);
+                v = g.alpha * v;
+                if (g.beta != 0.0 && rvalid && col0 + c0 + j < g.M)
+                  v = fma(g.beta, g.Cin[row * g.ldcin + col0 + c0 + j], v);
+                if constexpr (Cfg::GSTATE) {
+                  S[j] = v;
+                } else if (rvalid && col0 + c0 + j < g.M) {
+                  const int64_t col = col0 + c0 + j;
+                  if (!g.symmetric) {
+                    g.C[row * g.ldc + col] = v;
+                  } else if (tm != tn || col >= row) {
+                    g.C[row * g.ldc + col] = v;
+                    g.C[col * g.ldc + row] = v;
+                  }
+                }
+              }
+            }
+          } else {
+          // ---- FP64 sums (the same sums to FP64 rounding, pair order)
+          const uint32_t sflip = g.alpha < 0.0 ? 0x80000000u : 0u;
 #pragma unroll
           for (int j = 0; j < CH; ++j) {
             double acc;
@@ -357,25 +470,48 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
             } else {
               acc = __hiloint2double((int)H[j], (int)L[j]);
             }
-            const int eb = s_eB[b * BN + c0 + j];
-            const double pj = (double)__uint_as_float(P[j]);
-            if (ea + eb >= -1022 && ea + eb <= 1023)
-              acc = fma(pj, g.alpha * __longlong_as_double((long long)(ea + eb + 1023) << 52), acc);
-            else  // outside the normal range: scale in two exact steps
-              acc = fma(pj * pow2d(ea), g.alpha * pow2d(eb), acc);
+            // one FP64 add per term; the term itself is built on the integer pipes
+            acc += scaled_term(P[j], ea + s_eB[b * BN + c0 + j], sflip);
             if constexpr (Cfg::GSTATE) {
               if (!last) __stcg(gst + (int64_t)(c0 + j) * kBM, acc);
+              S[j] = acc;
             } else {
               L[j] = (uint32_t)__double2loint(acc);
               H[j] = (uint32_t)__double2hiint(acc);
             }
-            if (last && rvalid && col0 + c0 + j < g.M) {
-              const int64_t col = col0 + c0 + j;
-              if (!g.symmetric) {
-                g.C[row * g.ldc + col] = acc;
-              } else if (tm != tn || col >= row) {
-                g.C[row * g.ldc + col] = acc;
-                g.C[col * g.ldc + row] = acc;
+            if constexpr (!Cfg::GSTATE) {
+              if (last && rvalid && col0 + c0 + j < g.M) {
+                const int64_t col = col0 + c0 + j;
+                if (!g.symmetric) {
+                  g.C[row * g.ldc + col] = acc;
+                } else if (tm != tn || col >= row) {
+                  g.C[row * g.ldc + col] = acc;
+                  g.C[col * g.ldc + row] = acc;
+                }
+              }
+            }
+          }
+          }
+          if constexpr (Cfg::GSTATE) {
+            if (last && rvalid) {
+              const int64_t cb = col0 + c0;
+              double* crow = g.C + row * g.ldc + cb;
+              if (!g.symmetric && g.c_vec && cb + CH <= g.M) {
+#pragma unroll
+                for (int j = 0; j < CH; j += 4) st_global_v4_f64(crow + j, S[j], S[j + 1], S[j + 2], S[j + 3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < CH; ++j) {
+                  const int64_t col = cb + j;
+                  if (col < g.M) {
+                    if (!g.symmetric) {
+                      crow[j] = S[j];
+                    } else if (tm != tn || col >= row) {
+                      crow[j] = S[j];
+                      g.C[col * g.ldc + row] = S[j];
+                    }
+                  }
+                }
               }
             }
           }
@@ -396,8 +532,20 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
           if constexpr (PAIR) mbar_arrive_cluster(acce_leader + buf * sizeof(uint64_t));
           else mbar_arrive(&acce[buf]);
         }
+        if (g.stats && warp == 2 && lane == 0) {
+          const long long e2 = clock64();
+          ep_wait += e1 - e0;
+          ep_busy += e2 - e1;
+          ++ep_pairs;
+        }
         ++acc_it;
       }
+    }
+    if (g.stats && warp == 2 && lane == 0) {
+      unsigned long long* st = g.stats + 8 * blockIdx.x;
+      st[4] = (unsigned long long)ep_wait;
+      st[5] = (unsigned long long)ep_busy;
+      st[6] = (unsigned long long)ep_pairs;
     }
   }
 
@@ -429,6 +577,19 @@ static bool stats_enabled() {
     v = (s && s[0] == '1') ? 1 : 0;
   }
   return v == 1;
+}
+
+// L2 prefetch distance of the TMA producer, in stages (OZK_GEMM_PREFETCH;
+// default 0 = off: measured on B200, prefetches issued by the producer thread
+// delay its loads more than they save).
+static int prefetch_distance() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("OZK_GEMM_PREFETCH");
+    v = s ? atoi(s) : 0;
+    if (v < 0) v = 0;
+  }
+  return v;
 }
 
 // CTA-pair tiles are the default for wide outputs; OZK_GEMM_PAIR=0 selects
@@ -499,8 +660,8 @@ static int launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const PairLis
   cfg.numAttrs = 1;
   GemmArgs gl = ga;
   if (stats_enabled()) {
-    if (!g_stats_dev[dev]) cudaMalloc(&g_stats_dev[dev], 4 * 1024 * sizeof(unsigned long long));
-    cudaMemsetAsync(g_stats_dev[dev], 0, 4 * 1024 * sizeof(unsigned long long), stream);
+    if (!g_stats_dev[dev]) cudaMalloc(&g_stats_dev[dev], 8 * 1024 * sizeof(unsigned long long));
+    cudaMemsetAsync(g_stats_dev[dev], 0, 8 * 1024 * sizeof(unsigned long long), stream);
     gl.stats = g_stats_dev[dev];
     g_stats_ctas[dev] = units * per;
     g_stats_last_dev = dev;
@@ -518,7 +679,7 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
                       const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
                       int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
                       double* C, int64_t ldc, float* products, double* state, size_t state_bytes,
-                      int32_t* status, cudaStream_t stream) {
+                      int rho, int32_t* status, cudaStream_t stream) {
   if (N == 0 || M == 0) return OZK_OK;
   if (n_pairs < 1 || n_pairs > OZK_MAX_PAIRS) return set_error(OZK_ERR_ARG, "n_pairs out of range");
   if (k_pad <= 0 || k_pad % OZK_KB) return set_error(OZK_ERR_ARG, "k_pad must be a positive multiple of 64");
@@ -526,11 +687,14 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
     return set_error(OZK_ERR_ARG, "slice counts out of range");
   for (int p = 0; p < n_pairs; ++p)
     if (pair_a[p] >= nA || pair_b[p] >= nB) return set_error(OZK_ERR_ARG, "pair index out of range");
-  if (mode != OZK_ACC_F64 && mode != OZK_ACC_PRODUCTS) return set_error(OZK_ERR_ARG, "bad mode");
-  if (mode == OZK_ACC_F64 && !C) return set_error(OZK_ERR_ARG, "C is NULL");
+  if (mode != OZK_ACC_F64 && mode != OZK_ACC_PRODUCTS && mode != OZK_ACC_FIXED)
+    return set_error(OZK_ERR_ARG, "bad mode");
+  if (mode != OZK_ACC_PRODUCTS && !C) return set_error(OZK_ERR_ARG, "C is NULL");
+  if (mode == OZK_ACC_FIXED && (rho < 1 || rho > 30))
+    return set_error(OZK_ERR_ARG, "OZK_ACC_FIXED needs the extraction rho");
   if (mode == OZK_ACC_PRODUCTS && !products) return set_error(OZK_ERR_ARG, "products is NULL");
   if (beta != 0.0 && !Cin) return set_error(OZK_ERR_ARG, "Cin is NULL with beta != 0");
-  if (symmetric && (N != M || SA != SB || eA != eB || mode != OZK_ACC_F64))
+  if (symmetric && (N != M || SA != SB || eA != eB || mode == OZK_ACC_PRODUCTS))
     return set_error(OZK_ERR_ARG, "symmetric mode needs one operand, N == M and FP64 output");
   if (N > (int64_t)1 << 31 || M > (int64_t)1 << 31) return set_error(OZK_ERR_ARG, "dimension too large");
   int rc = get_encode_fn();
@@ -542,7 +706,7 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
   // scratch) for large FP64 outputs; 256 x 128 on CTA pairs (sums in TMEM)
   // when no scratch is given; narrow single-CTA tiles for narrow outputs
   // (e.g. residual right-hand sides).
-  const bool wide = mode == OZK_ACC_F64 && N >= 256 && M >= 256 && state &&
+  const bool wide = mode != OZK_ACC_PRODUCTS && N >= 256 && M >= 256 && state &&
                     state_bytes >= gemm_state_bytes(dev) && pair_mode_enabled();
   const int BN = wide ? 256 : (M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128)));
   const int bn = (symmetric && !wide) ? 128 : BN;
@@ -583,6 +747,11 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
   ga.status = status;
   ga.budget_ns = wait_budget_ns();
   ga.state = state;
+  ga.c_vec = C && ((uintptr_t)C % 32 == 0) && (ldc % 4 == 0);
+  ga.fixed = mode == OZK_ACC_FIXED;
+  ga.fix_off = -150 - 2 * (rho - 24) + kFixFrac;
+  ga.fix_scale = 2 * (rho - 24) - kFixFrac;
+  ga.prefetch = prefetch_distance();
   if (wide) return launch_bn<256, true>(ma, mb, pl, ga, dev, stream);
   switch (bn) {
     case 16: return launch_bn<16, false>(ma, mb, pl, ga, dev, stream);
@@ -596,16 +765,16 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
 
 }  // namespace ozk
 
-extern "C" int ozk_gemm_stats(unsigned long long* out4) {
+extern "C" int ozk_gemm_stats(unsigned long long* out8) {
   using namespace ozk;
-  if (!out4) return OZK_ERR_ARG;
-  for (int i = 0; i < 4; ++i) out4[i] = 0;
+  if (!out8) return OZK_ERR_ARG;
+  for (int i = 0; i < 8; ++i) out8[i] = 0;
   const int dev = g_stats_last_dev;
   if (dev < 0 || !g_stats_dev[dev]) return OZK_ERR_UNSUPPORTED;
-  unsigned long long h[4 * 1024];
+  static unsigned long long h[8 * 1024];
   cudaDeviceSynchronize();
   cudaMemcpy(h, g_stats_dev[dev], sizeof(h), cudaMemcpyDeviceToHost);
   for (int c = 0; c < g_stats_ctas[dev] && c < 1024; ++c)
-    for (int i = 0; i < 4; ++i) out4[i] += h[4 * c + i];
+    for (int i = 0; i < 8; ++i) out8[i] += h[8 * c + i];
   return g_stats_ctas[dev];
 }

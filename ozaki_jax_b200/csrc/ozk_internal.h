@@ -43,7 +43,7 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
                       const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
                       int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
                       double* C, int64_t ldc, float* products, double* state, size_t state_bytes,
-                      int32_t* status, cudaStream_t stream);
+                      int rho, int32_t* status, cudaStream_t stream);
 // Bytes of the per-CTA FP64 state scratch the 256-wide GEMM tiles need.
 size_t gemm_state_bytes(int dev);
 // Smallest workspace ozk_matmul_f64 (OZK_ACC_F64) accepts: without the state

@@ -70,6 +70,6 @@ extern "C" int ozk_matmul_f64_noalloc(const double* A, int64_t lda, const double
   void* scratch = nullptr;
   int rc = scratch_for_current_device(&scratch);
   if (rc) return rc;
-  return ozk_matmul_f64(A, lda, B, ldb, C, ldc, N, K, M, -1, n_hi, n_lo, OZK_ACC_F64, scratch,
+  return ozk_matmul_f64(A, lda, B, ldb, C, ldc, N, K, M, -1, n_hi, n_lo, OZK_ACC_FIXED, scratch,
                         (size_t)OZK_NOALLOC_SCRATCH_BYTES, status_dev, stream);
 }

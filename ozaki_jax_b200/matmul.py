@@ -9,10 +9,18 @@ as sm_100a kernels of libozaki_b200.so:
   slice GEMM (K2) persistent tcgen05/TMEM kernel over the pair schedule with
                  the scaled accumulation fused into its epilogue.
 
-accumulation='fused' / 'bf16_interleaved' / 'host' use the FP64 epilogue
-(FP64 running sum of the exact per-pair products); 'ondevice' materialises
-the products and applies the reference's FP32 2Sum in the reference's order,
-which reproduces the reference's fused result bit for bit.
+Accumulation of the exact per-pair products (the `accumulation` argument):
+  'fused', 'bf16_interleaved'  exact int64 fixed-point sums per element (unit
+                               2^-36 of the top slices' product grid), rounded
+                               to FP64 once -- no FP64 work per pair, which
+                               keeps the tensor cores fed; its resolution
+                               (about 2^-50 * max|A[r,:]| * max|B[:,c]|) is far
+                               below the Ozaki truncation error of every preset;
+  'host'                       FP64 sums in pair order: the semantics of the
+                               reference's FP64 host accumulation;
+  'ondevice'                   materialised products + the reference's FP32 2Sum
+                               in the reference's order: the reference's fused /
+                               ondevice result bit for bit.
 """
 
 import numpy as np
@@ -154,7 +162,8 @@ def _ondevice_device(Ad, Bd, n_hi, n_lo, accumulation, rho=None, out=None):
     dev = Ad.device
     C = out if out is not None else torch.empty((N, M), dtype=torch.float64, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    mode = L.OZK_ACC_PRODUCTS if accumulation == "ondevice" else L.OZK_ACC_F64
+    mode = {"ondevice": L.OZK_ACC_PRODUCTS, "host": L.OZK_ACC_F64}.get(accumulation,
+                                                                       L.OZK_ACC_FIXED)
     ws_bytes = lib.ozk_matmul_workspace_bytes(N, K, M, n_hi, n_lo)
     if mode == L.OZK_ACC_PRODUCTS:
         ws_bytes += (n_hi * n_hi + 2 * n_hi * n_lo) * N * M * 4 + 256

@@ -46,7 +46,7 @@ def run_products(SA, SB, eA, eB, k_pad, n_hi, n_lo):
     st = torch.zeros(1, dtype=torch.int32, device="cuda")
     rc = L.load().ozk_slice_gemm(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(), eB.data_ptr(),
                                  nS, N, M, k_pad, pa, pb, n, L.OZK_ACC_PRODUCTS, 0, 1.0, 0.0,
-                                 None, 0, None, 0, P.data_ptr(), None, 0, st.data_ptr(),
+                                 None, 0, None, 0, P.data_ptr(), None, 0, 0, st.data_ptr(),
                                  torch.cuda.current_stream().cuda_stream)
     L.check(rc)
     torch.cuda.synchronize()
@@ -86,7 +86,7 @@ def test_products_exact_at_the_bound():
     P = torch.empty((1, N, M), dtype=torch.float32, device="cuda")
     L.check(L.load().ozk_slice_gemm(SA.data_ptr(), e.data_ptr(), 1, SB.data_ptr(), e.data_ptr(), 1,
                                     N, M, K, pa, pb, 1, L.OZK_ACC_PRODUCTS, 0, 1.0, 0.0, None, 0,
-                                    None, 0, P.data_ptr(), None, 0, None,
+                                    None, 0, P.data_ptr(), None, 0, 0, None,
                                     torch.cuda.current_stream().cuda_stream))
     exact = sa[0].astype(np.float64) @ sb[0].astype(np.float64).T
     got = P.cpu().numpy()[0].astype(np.float64)
@@ -132,13 +132,16 @@ def test_accumulate_2sum_words_bit_exact(golden):
             assert same_bits(cl.cpu().numpy(), arrays[f"{name}/{pname}/C_lo"])
 
 
-@pytest.mark.parametrize("name", ["n64_s0", "rect_37x100x23", "zeros_24x48x16",
-                                  "wide_phi10_40x96x32", "k1040_8x1040x8", "vec_1x128x1",
-                                  "outer_48x1x40"])
+FP64_CASES = ["n64_s0", "rect_37x100x23", "zeros_24x48x16", "wide_phi10_40x96x32",
+              "k1040_8x1040x8", "vec_1x128x1", "outer_48x1x40"]
+
+
+@pytest.mark.parametrize("name", FP64_CASES)
 def test_fp64_epilogue_matches_fp64_oracle(golden, name):
-    """The fused FP64 epilogue agrees with the reference's FP64-accumulating
-    NumPy pipeline (matmul_numpy, goldens) to FP64 rounding: the two differ
-    only in the order of exact-product additions."""
+    """accumulation='host' (FP64 sums) agrees with the reference's
+    FP64-accumulating NumPy pipeline (matmul_numpy, goldens) to FP64 rounding
+    element by element: the two differ only in the order of exact-product
+    additions."""
     from ozaki_jax_b200.matmul import _ondevice_device
     arrays, _ = golden
     A, B = arrays[f"{name}/A"], arrays[f"{name}/B"]
@@ -148,14 +151,41 @@ def test_fp64_epilogue_matches_fp64_oracle(golden, name):
         if key not in arrays:
             continue
         C, _ = _ondevice_device(torch.as_tensor(A).cuda(), torch.as_tensor(B).cuda(), n_hi, n_lo,
-                                "fused")
+                                "host")
         C = C.cpu().numpy()
         ref = arrays[key]
-        # distance to the FP64-accumulating reference: rounding level of |A||B|
         scale = np.abs(A) @ np.abs(B)
         assert np.all(np.abs(C - ref) <= 64 * 2.0 ** -52 * scale + 1e-300), pname
         # accuracy no worse than 1.5x the reference's; below 32 ulps of FP64 the
         # Ozaki truncation is gone and only FP64 summation order remains
+        e_ref = min(O.rel_err(ref, E), O.rel_err(arrays[f"{name}/{pname}/fused"], E))
+        assert O.rel_err(C, E) <= max(1.5 * e_ref, 32 * 2.0 ** -52), pname
+
+
+@pytest.mark.parametrize("name", FP64_CASES)
+def test_fixed_point_epilogue_error_model(golden, name):
+    """accumulation='fused' (exact int64 fixed-point sums): normwise accuracy
+    no worse than 1.5x the reference's, and element by element within the
+    fixed-point resolution of the reference's FP64 pipeline -- a few units of
+    2^-50 * max|A[r,:]| * max|B[:,c]| per term (the same row/column-max scale
+    the Ozaki truncation error has)."""
+    from ozaki_jax_b200.matmul import _ondevice_device
+    arrays, _ = golden
+    A, B = arrays[f"{name}/A"], arrays[f"{name}/B"]
+    E = O.exact_product(A, B)
+    rmax = np.max(np.abs(A), axis=1)[:, None]
+    cmax = np.max(np.abs(B), axis=0)[None, :]
+    for pname, (n_hi, n_lo) in PRESETS.items():
+        key = f"{name}/{pname}/numpy"
+        if key not in arrays:
+            continue
+        C, _ = _ondevice_device(torch.as_tensor(A).cuda(), torch.as_tensor(B).cuda(), n_hi, n_lo,
+                                "fused")
+        C = C.cpu().numpy()
+        ref = arrays[key]
+        n_pairs = n_hi * n_hi + 2 * n_hi * n_lo
+        bound = n_pairs * 2.0 ** -48 * rmax * cmax + 64 * 2.0 ** -52 * (np.abs(A) @ np.abs(B))
+        assert np.all(np.abs(C - ref) <= bound + 1e-300), pname
         e_ref = min(O.rel_err(ref, E), O.rel_err(arrays[f"{name}/{pname}/fused"], E))
         assert O.rel_err(C, E) <= max(1.5 * e_ref, 32 * 2.0 ** -52), pname
 

@@ -75,7 +75,7 @@ def test_argument_errors_return_codes():
                               None) == _lib.OZK_ERR_ARG
     assert lib.ozk_pair_schedule(0, 1, None, None, 0) == _lib.OZK_ERR_ARG
     assert lib.ozk_slice_gemm(None, None, 1, None, None, 1, 1, 1, 64, None, None, 1, 0, 0, 1.0,
-                              0.0, None, 0, None, 0, None, None, 0, None, None) == _lib.OZK_ERR_ARG
+                              0.0, None, 0, None, 0, None, None, 0, 0, None, None) == _lib.OZK_ERR_ARG
     assert "NULL" in _lib.detail()
 
 

@@ -32,14 +32,16 @@ def _call_noalloc(lib, Ad, Bd, n_hi, n_lo):
 
 
 def _call_allocating(lib, Ad, Bd, n_hi, n_lo):
+    from ozaki_jax_b200 import _lib
     N, K = Ad.shape
     M = Bd.shape[1]
     C = torch.empty((N, M), dtype=torch.float64, device="cuda")
     st = torch.zeros(1, dtype=torch.int32, device="cuda")
     ws_bytes = lib.ozk_matmul_workspace_bytes(N, K, M, n_hi, n_lo)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    # same accumulation as the allocation-free entry point: 'fused' (OZK_ACC_FIXED)
     rc = lib.ozk_matmul_f64(Ad.data_ptr(), K, Bd.data_ptr(), M, C.data_ptr(), M, N, K, M, -1,
-                            n_hi, n_lo, 0, ws.data_ptr(), ws_bytes, st.data_ptr(),
+                            n_hi, n_lo, _lib.OZK_ACC_FIXED, ws.data_ptr(), ws_bytes, st.data_ptr(),
                             torch.cuda.current_stream().cuda_stream)
     return rc, C, st
 

@@ -226,6 +226,11 @@ int ozk_last_error_detail(char* buf, size_t len);
  * (epilogue figures from one warp per CTA); returns the CTA count
  * (synchronises the device). */
 int ozk_gemm_stats(unsigned long long* out8);
+/* Failure-path self-test (no counterpart in the reference): one CTA waits on an
+ * mbarrier nothing arrives at, through the bounded wait all kernels use; after
+ * budget_ms the wait gives up, writes 0 to *ok_dev and raises
+ * OZK_FLAG_TIMEOUT in *status_dev.  No fault, no hang. */
+int ozk_selftest_timeout(int budget_ms, int32_t* status_dev, int32_t* ok_dev, void* stream);
 /* Library version string. */
 const char* ozk_version(void);
 

@@ -70,6 +70,7 @@ SIGNATURES = {
                                  c_int, c_int, c_int, vp, c_size, vp, vp]),
     "ozk_check_status": (c_int, [vp, vp]),
     "ozk_gemm_stats": (c_int, [vp]),
+    "ozk_selftest_timeout": (c_int, [c_int, vp, vp, vp]),
     "ozk_strerror": (ctypes.c_char_p, [c_int]),
     "ozk_last_error_detail": (c_int, [ctypes.c_char_p, c_size]),
     "ozk_version": (ctypes.c_char_p, []),

@@ -155,6 +155,26 @@ __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, i
                : "memory");
 }
 
+// L2 cache policy that keeps lines resident (evict_last) for data re-read soon.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ long long ld_l2_hint(const long long* p, uint64_t pol) {
+  long long v;
+  asm volatile("ld.global.L1::no_allocate.L2::cache_hint.b64 %0, [%1], %2;"
+               : "=l"(v)
+               : "l"(p), "l"(pol)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_l2_hint(long long* p, long long v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.b64 [%0], %1, %2;" ::"l"(p), "l"(v), "l"(pol) : "memory");
+}
+
 // 32-byte vector store (sm_100): p must be 32-byte aligned.
 __device__ __forceinline__ void st_global_v4_f64(double* p, double a, double b, double c, double d) {
   asm volatile("st.global.v4.f64 [%0], {%1, %2, %3, %4};" ::"l"(p), "d"(a), "d"(b), "d"(c), "d"(d)

@@ -347,6 +347,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
     // one column (256 contiguous bytes) per access.
     double* const gst = Cfg::GSTATE ? g.state + (int64_t)blockIdx.x * Cfg::STATE_PER_CTA
                                       + q * 32 + lane : nullptr;
+    const uint64_t l2keep = l2_policy_evict_last();  // the state is re-read every pair
     const uint32_t acce_leader = PAIR ? mapa_u32(&acce[0], 0) : 0;
     uint32_t acc_it = 0;
     bool ok = true;
@@ -406,7 +407,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
           if constexpr (Cfg::GSTATE) {
             if (!first) {
 #pragma unroll
-              for (int j = 0; j < CH; ++j) S[j] = __ldcg(gst + (int64_t)(c0 + j) * kBM);
+              for (int j = 0; j < CH; ++j)
+                S[j] = __longlong_as_double(
+                    ld_l2_hint((const long long*)(gst + (int64_t)(c0 + j) * kBM), l2keep));
             }
           }
           tmem_wait_ld();
@@ -432,7 +435,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
               }
               if (!last) {
                 if constexpr (Cfg::GSTATE) {
-                  __stcg(gst + (int64_t)(c0 + j) * kBM, __longlong_as_double(acc));
+                  st_l2_hint((long long*)(gst + (int64_t)(c0 + j) * kBM), acc, l2keep);
                 } else {
                   L[j] = (uint32_t)acc;
                   H[j] = (uint32_t)((unsigned long long)acc >> 32);
@@ -473,7 +476,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
             // one FP64 add per term; the term itself is built on the integer pipes
             acc += scaled_term(P[j], ea + s_eB[b * BN + c0 + j], sflip);
             if constexpr (Cfg::GSTATE) {
-              if (!last) __stcg(gst + (int64_t)(c0 + j) * kBM, acc);
+              if (!last)
+                st_l2_hint((long long*)(gst + (int64_t)(c0 + j) * kBM), __double_as_longlong(acc),
+                           l2keep);
               S[j] = acc;
             } else {
               L[j] = (uint32_t)__double2loint(acc);
@@ -777,4 +782,39 @@ extern "C" int ozk_gemm_stats(unsigned long long* out8) {
   for (int c = 0; c < g_stats_ctas[dev] && c < 1024; ++c)
     for (int i = 0; i < 8; ++i) out8[i] += h[8 * c + i];
   return g_stats_ctas[dev];
+}
+
+// ---------------------------------------------------------------- self-test
+
+namespace ozk {
+
+// One CTA waits, through the same bounded wait every kernel uses, on an
+// mbarrier that nothing arrives at; the wait gives up after budget_ns and
+// raises OZK_FLAG_TIMEOUT.  Exercises the timeout path without a fault.
+__global__ void k_selftest_timeout(int32_t* status, uint64_t budget_ns, int32_t* out_ok) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = mbar_wait(&bar, 0, &abort_flag, status, budget_ns);
+    *out_ok = ok ? 1 : 0;
+  }
+}
+
+}  // namespace ozk
+
+extern "C" int ozk_selftest_timeout(int budget_ms, int32_t* status_dev, int32_t* ok_dev,
+                                    void* stream) {
+  using namespace ozk;
+  if (!status_dev || !ok_dev || budget_ms < 1 || budget_ms > 10000)
+    return set_error(OZK_ERR_ARG, "bad self-test arguments");
+  k_selftest_timeout<<<1, 32, 0, (cudaStream_t)stream>>>(status_dev, (uint64_t)budget_ms * 1000000ull,
+                                                        ok_dev);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OZK_OK : set_cuda_error("k_selftest_timeout launch", e);
 }

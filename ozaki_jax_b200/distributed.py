@@ -1,0 +1,128 @@
+"""Row-sharded Ozaki matmul over the GPUs of one node (one process per GPU).
+
+The reference has no multi-device code; this is the build's partitioning of
+the on-device path.  Rank r owns rows [r*N/P, (r+1)*N/P) of A and of C.  Row
+extraction is row-local, so each rank's slices of A are bit-identical to the
+single-GPU ones and each rank's block of C equals the corresponding rows of
+the single-GPU result.  B reaches every rank in one of two ways:
+
+  b_source='replicated'  every rank was given B and extracts its column slices
+                         locally (no collective in the data path);
+  b_source='root'        rank 0 extracts B's slices once and broadcasts the BF16
+                         slice stack and exponents over NCCL (NVLink).
+
+The collectives go through torch.distributed (NCCL for CUDA tensors, gloo on
+CPU); the compute is libozaki_b200.
+"""
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _device as D
+from . import _lib as L
+from .matmul import _resolve_precision, compute_rho_f32
+
+
+def row_range(n, rank, world):
+    """Rows [r0, r1) of an n-row matrix owned by `rank` of `world`."""
+    return rank * n // world, (rank + 1) * n // world
+
+
+def broadcast_(t, src=0, group=None):
+    """In-place broadcast of a tensor from `src` (thin wrapper, kept for tests)."""
+    dist.broadcast(t, src=src, group=group)
+    return t
+
+
+def gather_rows(C_local, n_total, dst=None, group=None):
+    """Assemble the row blocks of C.  Blocks may differ in size by one row, so
+    each is padded to the largest block for the collective.  dst=None gathers on
+    every rank (all_gather); otherwise only rank `dst` returns the full C."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    sizes = [row_range(n_total, r, world) for r in range(world)]
+    mx = max(r1 - r0 for r0, r1 in sizes)
+    pad = torch.zeros((mx,) + tuple(C_local.shape[1:]), dtype=C_local.dtype,
+                      device=C_local.device)
+    pad[: C_local.shape[0]] = C_local
+    if dst is None:
+        parts = [torch.empty_like(pad) for _ in range(world)]
+        dist.all_gather(parts, pad, group=group)
+    else:
+        parts = [torch.empty_like(pad) for _ in range(world)] if rank == dst else None
+        dist.gather(pad, gather_list=parts, dst=dst, group=group)
+        if rank != dst:
+            return None
+    return torch.cat([p[: r1 - r0] for p, (r0, r1) in zip(parts, sizes)], dim=0)
+
+
+def _pairs(lib, n_hi, n_lo):
+    pa = (ctypes.c_uint8 * 256)()
+    pb = (ctypes.c_uint8 * 256)()
+    n = L.check(lib.ozk_pair_schedule_snake(n_hi, n_lo, pa, pb, 256))
+    return pa, pb, n
+
+
+def matmul_rowsharded(A_local, B, K=None, precision="high", b_source="replicated", group=None):
+    """C_local = (A @ B)[rows of this rank] with the Ozaki 'fused' accumulation.
+
+    A_local: this rank's row block of A (CUDA float64, rows x K).
+    B: the full K x M matrix on every rank ('replicated'), or a K x M tensor
+       whose contents matter only on rank 0 ('root'; other ranks may pass a
+       tensor of the right shape or None with K given through A_local).
+    Returns this rank's rows of C (CUDA float64).  All ranks must call it.
+    """
+    lib = L.load()
+    n_hi, n_lo = _resolve_precision(precision)
+    nS = n_hi + n_lo
+    dev = A_local.device
+    rank = dist.get_rank(group)
+    Ad = A_local.to(dtype=torch.float64).contiguous()
+    nb, Kd = Ad.shape
+    if b_source not in ("replicated", "root"):
+        raise ValueError("b_source must be 'replicated' or 'root'")
+    shape = torch.tensor(list(B.shape) if (B is not None and rank == 0) else [0, 0],
+                         dtype=torch.int64, device=dev)
+    if b_source == "root":
+        dist.broadcast(shape, src=0, group=group)
+        Kb, M = int(shape[0]), int(shape[1])
+    else:
+        Kb, M = B.shape
+    if Kb != Kd:
+        raise ValueError(f"Incompatible shapes for matmul: {tuple(Ad.shape)} and {(Kb, M)}.")
+    rho = compute_rho_f32(Kd)
+    k_pad = (max(Kd, 1) + 63) // 64 * 64
+    sh = D.stream_handle(dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    SB = torch.empty((nS, M, k_pad), dtype=torch.int16, device=dev)
+    eB = torch.empty((nS, M), dtype=torch.int32, device=dev)
+    if b_source == "replicated" or rank == 0:
+        Bd = B.to(device=dev, dtype=torch.float64).contiguous()
+        BT = torch.empty((M, Kd), dtype=torch.float64, device=dev)
+        L.check(lib.ozk_extract_cols_f64(Bd.data_ptr(), Bd.stride(0), Kd, M, rho, n_hi, n_lo,
+                                         SB.data_ptr(), k_pad, eB.data_ptr(), BT.data_ptr(),
+                                         BT.numel() * 8, status.data_ptr(), sh))
+    if b_source == "root":
+        dist.broadcast(SB, src=0, group=group)
+        dist.broadcast(eB, src=0, group=group)
+    SA = torch.empty((nS, nb, k_pad), dtype=torch.int16, device=dev)
+    eA = torch.empty((nS, nb), dtype=torch.int32, device=dev)
+    C = torch.empty((nb, M), dtype=torch.float64, device=dev)
+    if nb > 0:
+        L.check(lib.ozk_extract_rows_f64(Ad.data_ptr(), Ad.stride(0), nb, Kd, rho, n_hi, n_lo,
+                                         SA.data_ptr(), k_pad, eA.data_ptr(), status.data_ptr(),
+                                         sh))
+        pa, pb, npairs = _pairs(lib, n_hi, n_lo)
+        GW = torch.empty(lib.ozk_slice_gemm_workspace_bytes(), dtype=torch.uint8, device=dev)
+        L.check(lib.ozk_slice_gemm(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(), eB.data_ptr(),
+                                   nS, nb, M, k_pad, pa, pb, npairs, L.OZK_ACC_FIXED, 0, 1.0, 0.0,
+                                   None, 0, C.data_ptr(), M, None, GW.data_ptr(), GW.numel(), rho,
+                                   status.data_ptr(), sh))
+    flags = int(status.item())
+    if flags:
+        raise ValueError("Ozaki preflight marked this input as unsafe: inputs contain NaN or Inf"
+                         if flags & (L.OZK_FLAG_NONFINITE | L.OZK_FLAG_RANGE)
+                         else f"device status {flags}")
+    return C

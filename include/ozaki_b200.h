@@ -134,6 +134,40 @@ int ozk_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t
  * that keep the sums in TMEM. */
 size_t ozk_slice_gemm_workspace_bytes(void);
 
+/* int8 slice codes (no counterpart in the reference: an exact re-encoding of
+ * its BF16 slices for the tensor cores' integer path).  Every slice of the
+ * on-device extraction is an integer multiple of 2^(rho-24) of magnitude at
+ * most 2^(25-rho); for rho >= 19 (K > 4096 with the reference's rho) the code
+ * q = slice * 2^(24-rho) is an exact int8 with |q| <= 64, and an int8 x int8
+ * MMA with int32 accumulation gives exactly the per-pair products the BF16
+ * slices give in FP32.  Same recurrence and exponents as
+ * ozk_extract_rows_f64 / ozk_extract_cols_f64; slices [n_hi+n_lo][lines][k_pad]
+ * int8 with k_pad a multiple of 128 (<= 65536).  A value without an exact code
+ * (slices of lines whose magnitude leaves the FP32 range the recurrence needs)
+ * sets *fail_dev = 1: the codes are then unusable and the BF16 entry points
+ * must be used.  The column form needs cols*K doubles of scratch (NULL: taken
+ * from the stream-ordered pool). */
+int ozk_extract_rows_s8_f64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                            int n_hi, int n_lo, int8_t* slices, int64_t k_pad, int32_t* exps,
+                            int32_t* fail_dev, int32_t* status_dev, void* stream);
+int ozk_extract_cols_s8_f64(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho,
+                            int n_hi, int n_lo, int8_t* slices, int64_t k_pad, int32_t* exps,
+                            double* scratch, size_t scratch_bytes, int32_t* fail_dev,
+                            int32_t* status_dev, void* stream);
+
+/* ozk_slice_gemm in OZK_ACC_FIXED mode on int8 slice codes (kind::i8 MMAs,
+ * int32 accumulators): the same C bit for bit as the BF16 slices give.  Needs
+ * rho >= 19, N and M >= 256, k_pad a multiple of 128 and a workspace of
+ * ozk_slice_gemm_workspace_bytes().  With skip_if_dev non-NULL the GEMM does
+ * nothing when *skip_if_dev != 0 (pass the extraction's fail word to keep a
+ * failed extraction from producing a result, without a host round trip). */
+int ozk_slice_gemm_s8(const int8_t* SA, const int32_t* eA, int nA, const int8_t* SB,
+                      const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
+                      const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int symmetric,
+                      double alpha, double beta, const double* Cin, int64_t ldcin, double* C,
+                      int64_t ldc, void* workspace, size_t ws_bytes, int rho,
+                      const int32_t* skip_if_dev, int32_t* status_dev, void* stream);
+
 /* Reference-order FP32 2Sum accumulation of materialised products
  * (accumulate_2sum / _accumulate_2sum_logic, ozaki_jax/pallas_ops.py:178-239,
  * :372-396, with the scales of _precompute_accumulation_scales, :107-175):
@@ -165,6 +199,25 @@ int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, d
                    int64_t ldc, int64_t N, int64_t K, int64_t M, int rho, int n_hi, int n_lo,
                    int acc_mode, void* workspace, size_t ws_bytes, int32_t* status_dev,
                    void* stream);
+
+/* The on-device pipeline called with HOST arrays (ozaki_jax.matmul on NumPy
+ * inputs with pipeline='ondevice', ozaki_jax/matmul.py:781-821 -> :641-686,
+ * where the arrays are transferred to the device, the jitted pipeline runs and
+ * the result comes back to the host): A, B, C are host pointers (pinned memory
+ * copies at full DMA speed; pageable memory works through the driver's
+ * staging).  The copies overlap the compute: B is copied and column-extracted
+ * first, then A and C move in row blocks of block_rows rows (0 = automatic) on
+ * two internal copy streams while the previous block's slice GEMM runs on
+ * `stream`.  Blocking: returns after C is written; *status_host receives the
+ * OZK_FLAG_* bits of the run (0 = clean).  acc_mode as for ozk_matmul_f64;
+ * workspace as sized by ozk_matmul_hostbuf_workspace_bytes, or NULL for the
+ * stream-ordered pool. */
+size_t ozk_matmul_hostbuf_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo,
+                                          int acc_mode, int64_t block_rows);
+int ozk_matmul_f64_hostbuf(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
+                           int64_t ldc, int64_t N, int64_t K, int64_t M, int rho, int n_hi,
+                           int n_lo, int acc_mode, int64_t block_rows, void* workspace,
+                           size_t ws_bytes, int32_t* status_host, void* stream);
 
 /* Allocation-free variant of ozk_matmul_f64 (acc_mode OZK_ACC_FIXED, rho from K).
  * It has no counterpart in the reference.  For callers that must not allocate
@@ -222,7 +275,8 @@ int ozk_last_error_detail(char* buf, size_t len);
  * {0: MMA-thread cycles waiting for a free accumulator, 1: MMA-thread cycles
  * waiting for loaded stages, 2: producer cycles waiting for free stages,
  * 3: MMA-thread total cycles, 4: epilogue cycles waiting for a finished
- * accumulator, 5: epilogue cycles processing, 6: epilogue pairs, 7: 0}
+ * accumulator, 5: epilogue cycles processing, 6: epilogue pairs, 7: the part
+ * of 1 spent in the first pipeline-depth k-blocks of each pair}
  * (epilogue figures from one warp per CTA); returns the CTA count
  * (synchronises the device). */
 int ozk_gemm_stats(unsigned long long* out8);
@@ -231,6 +285,17 @@ int ozk_gemm_stats(unsigned long long* out8);
  * budget_ms the wait gives up, writes 0 to *ok_dev and raises
  * OZK_FLAG_TIMEOUT in *status_dev.  No fault, no hang. */
 int ozk_selftest_timeout(int budget_ms, int32_t* status_dev, int32_t* ok_dev, void* stream);
+/* L2 residency of the slice GEMM's running sums (no counterpart in the
+ * reference).  The 256-wide GEMM tiles keep per-CTA running sums in a global
+ * scratch (ozk_slice_gemm_workspace_bytes, about 37 MB) that it re-reads every
+ * pair, and it marks those accesses evict_last.  That priority takes effect
+ * only inside the context's persisting-L2 set-aside, which is 0 by default.
+ * This sets the set-aside of the current device's context to `bytes` (clamped
+ * to the device maximum; 0 turns it off) and returns the value in force
+ * before in *previous (may be NULL).  The limit belongs to this process's CUDA
+ * context and ends with it; it reduces the L2 left to other kernels of the
+ * process by the same amount. */
+int ozk_set_l2_persisting(size_t bytes, size_t* previous);
 /* Library version string. */
 const char* ozk_version(void);
 

@@ -50,6 +50,15 @@ def to_device_f64(x, device):
     return host.to(device, non_blocking=True)
 
 
+def host_empty_f64(shape):
+    """Uninitialised float64 NumPy array; page-locked (from torch's pinned host
+    pool) when large, so device-to-host copies into it run as DMA."""
+    n = int(np.prod(shape)) if len(shape) else 1
+    if n >= (1 << 17) and torch.cuda.is_available():
+        return torch.empty(tuple(shape), dtype=torch.float64, pin_memory=True).numpy()
+    return np.empty(shape, dtype=np.float64)
+
+
 def to_host_f64(t):
     """NumPy float64 array with the values of the CUDA tensor t (blocking)."""
     if t.numel() >= (1 << 17):

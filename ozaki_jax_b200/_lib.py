@@ -52,11 +52,23 @@ SIGNATURES = {
                                c_int, c_int, c_dbl, c_dbl, vp, c_i64, vp, c_i64, vp, vp, c_size,
                                c_int, vp, vp]),
     "ozk_slice_gemm_workspace_bytes": (c_size, []),
+    "ozk_extract_rows_s8_f64": (c_int, [vp, c_i64, c_i64, c_i64, c_int, c_int, c_int, vp, c_i64,
+                                        vp, vp, vp, vp]),
+    "ozk_extract_cols_s8_f64": (c_int, [vp, c_i64, c_i64, c_i64, c_int, c_int, c_int, vp, c_i64,
+                                        vp, vp, c_size, vp, vp, vp]),
+    "ozk_slice_gemm_s8": (c_int, [vp, vp, c_int, vp, vp, c_int, c_i64, c_i64, c_i64, vp, vp, c_int,
+                                  c_int, c_dbl, c_dbl, vp, c_i64, vp, c_i64, vp, c_size, c_int, vp,
+                                  vp, vp]),
     "ozk_accumulate_2sum": (c_int, [vp, vp, vp, c_i64, c_i64, c_int, c_int, vp, vp, vp, c_i64,
                                     vp]),
     "ozk_matmul_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_int, c_int]),
     "ozk_matmul_f64": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64, c_int, c_int,
                                c_int, c_int, vp, c_size, vp, vp]),
+    "ozk_matmul_hostbuf_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_int, c_int, c_int,
+                                                    c_i64]),
+    "ozk_matmul_f64_hostbuf": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64, c_int,
+                                       c_int, c_int, c_int, c_i64, vp, c_size, vp, vp]),
+    "ozk_set_l2_persisting": (c_int, [c_size, vp]),
     "ozk_matmul_f64_noalloc": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64,
                                        c_int, c_int, vp, vp]),
     "ozk_matmul_host_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_int]),

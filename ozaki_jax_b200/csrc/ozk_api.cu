@@ -69,7 +69,7 @@ static int rho_f64(int64_t K) {  // extract.py:12-18
 
 // BF16 -> FP32 exact inner-product bound K * (2^bits - 1)^2 < 2^24
 // (matmul.py:605-621 and :84-97).
-static int check_bound(int64_t K, int bits) {
+int check_bound(int64_t K, int bits) {
   if (bits <= 0)
     return set_error(OZK_ERR_UNSAFE, "non-positive bits per slice (%d); K=%lld is too large", bits,
                      (long long)K);
@@ -135,6 +135,7 @@ struct Workspace {
   float* products;
   double* state;  // per-CTA FP64 running sums of the 256-wide GEMM tiles
   size_t state_bytes;
+  int32_t* gate;  // set when an int8 slice code failed: the BF16 recomputation runs
   size_t bytes;
 };
 
@@ -142,7 +143,8 @@ static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // Layout: SA [nS][N][k_pad] | SB [nS][M][k_pad] | eA [nS][N] | eB [nS][M] |
 // BT [bt_elems] FP64 | products [n_pairs][N][M] (only when materialised) |
-// state [state_bytes] (optional GEMM scratch).
+// state [state_bytes] (optional GEMM scratch) | gate word.  The slice areas
+// are sized for BF16; int8 codes use the first half of each.
 static Workspace layout(void* base, int64_t N, int64_t K, int64_t M, int nS, int n_prod,
                         int64_t bt_elems, size_t state_bytes = 0) {
   const int64_t k_pad = round_up(K < 1 ? 1 : K, OZK_KB);
@@ -164,6 +166,8 @@ static Workspace layout(void* base, int64_t N, int64_t K, int64_t M, int nS, int
   w.state = state_bytes ? (double*)(b + off) : nullptr;
   w.state_bytes = state_bytes;
   off += align256(state_bytes);
+  w.gate = (int32_t*)(b + off);
+  off += 256;
   w.bytes = off;
   return w;
 }
@@ -212,6 +216,64 @@ static int pick_workspace(void* given, size_t given_bytes, size_t full, size_t m
 
 size_t matmul_min_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo) {
   return layout(nullptr, N, K, M, n_hi + n_lo, 0, M * K).bytes;
+}
+
+// int8 slices for fixed-point sums where eligible (OZK_S8=0 in the
+// environment turns them off, for comparisons).
+bool s8_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("OZK_S8");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// C = A B with fixed-point sums.  Where the int8 GEMM applies, the slices are
+// extracted as int8 codes and multiplied with kind::i8 MMAs; the BF16
+// extraction and GEMM are enqueued behind them gated on w.gate, so they run
+// (and overwrite the result) only if some slice had no exact int8 code.  The
+// stream never waits on the host for that decision.
+static int matmul_fixed(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
+                        int64_t ldc, int64_t N, int64_t K, int64_t M, int rho, int n_hi, int n_lo,
+                        const uint8_t* pa, const uint8_t* pb, int np, const Workspace& w,
+                        int32_t* status_dev, cudaStream_t s) {
+  const int nS = n_hi + n_lo;
+  const int64_t k_pad = round_up(K, OZK_KB);
+  const int64_t k8 = round_up(K, kS8KB);
+  int rc;
+  if (!s8_enabled() || !slice_gemm_s8_eligible(N, M, k8, OZK_ACC_FIXED, rho, w.state_bytes)) {
+    if ((rc = launch_extract_rows(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
+      return rc;
+    if ((rc = launch_extract_cols(B, ldb, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev,
+                                  w.BT, s)))
+      return rc;
+    return launch_slice_gemm(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np,
+                             OZK_ACC_FIXED, 0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, w.state,
+                             w.state_bytes, rho, status_dev, s);
+  }
+  cudaError_t e = cudaMemsetAsync(w.gate, 0, sizeof(int32_t), s);
+  if (e != cudaSuccess) return set_cuda_error("cudaMemsetAsync(gate)", e);
+  if ((rc = launch_extract_rows_s8(A, lda, N, K, rho, n_hi, n_lo, (int8_t*)w.SA, k8, w.eA,
+                                   status_dev, w.gate, s)))
+    return rc;
+  if ((rc = launch_extract_cols_s8(B, ldb, K, M, rho, n_hi, n_lo, (int8_t*)w.SB, k8, w.eB,
+                                   status_dev, w.gate, w.BT, s)))
+    return rc;
+  if ((rc = launch_slice_gemm_ex(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k8, pa, pb, np,
+                                 OZK_ACC_FIXED, 0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, w.state,
+                                 w.state_bytes, rho, status_dev, true, w.gate, 0, s)))
+    return rc;
+  // BF16 recomputation (B from its transposed copy), only if the gate is set.
+  if ((rc = launch_extract_rows_gated(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev,
+                                      w.gate, s)))
+    return rc;
+  if ((rc = launch_extract_rows_gated(w.BT, K, M, K, rho, n_hi, n_lo, w.SB, k_pad, w.eB,
+                                      status_dev, w.gate, s)))
+    return rc;
+  return launch_slice_gemm_ex(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np,
+                              OZK_ACC_FIXED, 0, 1.0, 0.0, nullptr, 0, C, ldc, nullptr, w.state,
+                              w.state_bytes, rho, status_dev, false, w.gate, 1, s);
 }
 
 }  // namespace ozk
@@ -332,6 +394,69 @@ int ozk_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t
 
 size_t ozk_slice_gemm_workspace_bytes(void) { return cur_state_bytes(); }
 
+static int check_s8_extract(int rho, int64_t k_pad, const int32_t* fail_dev) {
+  if (!fail_dev) return set_error(OZK_ERR_ARG, "fail_dev is NULL");
+  if (rho < kS8MinRho)
+    return set_error(OZK_ERR_UNSUPPORTED, "int8 slice codes need rho >= %d (got %d)", kS8MinRho, rho);
+  if (k_pad % kS8KB || k_pad > 65536)
+    return set_error(OZK_ERR_ARG, "k_pad must be a multiple of %d, at most 65536", kS8KB);
+  return OZK_OK;
+}
+
+int ozk_extract_rows_s8_f64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                            int n_hi, int n_lo, int8_t* slices, int64_t k_pad, int32_t* exps,
+                            int32_t* fail_dev, int32_t* status_dev, void* stream) {
+  int rc = check_extract_args(X, ldx, rows, K, K, n_hi, n_lo, slices, k_pad, exps);
+  if (rc) return rc;
+  if (rho < 0) rho = rho_f32(K);
+  if ((rc = check_s8_extract(rho, k_pad, fail_dev))) return rc;
+  return launch_extract_rows_s8(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status_dev,
+                                fail_dev, (cudaStream_t)stream);
+}
+
+int ozk_extract_cols_s8_f64(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho,
+                            int n_hi, int n_lo, int8_t* slices, int64_t k_pad, int32_t* exps,
+                            double* scratch, size_t scratch_bytes, int32_t* fail_dev,
+                            int32_t* status_dev, void* stream) {
+  int rc = check_extract_args(X, ldx, cols, K, cols, n_hi, n_lo, slices, k_pad, exps);
+  if (rc) return rc;
+  if (rho < 0) rho = rho_f32(K);
+  if ((rc = check_s8_extract(rho, k_pad, fail_dev))) return rc;
+  const size_t need = (size_t)cols * K * 8;
+  if (scratch && scratch_bytes < need)
+    return set_error(OZK_ERR_WORKSPACE, "scratch %zu bytes < %zu needed", scratch_bytes, need);
+  ScopedWs ws;
+  if (!scratch && cols > 0) {
+    if ((rc = ws.acquire(nullptr, 0, need, (cudaStream_t)stream))) return rc;
+    scratch = (double*)ws.ptr;
+  }
+  return launch_extract_cols_s8(X, ldx, K, cols, rho, n_hi, n_lo, slices, k_pad, exps, status_dev,
+                                fail_dev, scratch, (cudaStream_t)stream);
+}
+
+int ozk_slice_gemm_s8(const int8_t* SA, const int32_t* eA, int nA, const int8_t* SB,
+                      const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
+                      const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int symmetric,
+                      double alpha, double beta, const double* Cin, int64_t ldcin, double* C,
+                      int64_t ldc, void* workspace, size_t ws_bytes, int rho,
+                      const int32_t* skip_if_dev, int32_t* status_dev, void* stream) {
+  if (!SA || !SB || !eA || !eB || !pair_a || !pair_b || !C)
+    return set_error(OZK_ERR_ARG, "NULL pointer");
+  if (N < 0 || M < 0) return set_error(OZK_ERR_ARG, "bad shape");
+  if (ldc < M) return set_error(OZK_ERR_ARG, "ldc < M");
+  if (beta != 0.0 && (!Cin || ldcin < M)) return set_error(OZK_ERR_ARG, "bad Cin");
+  if (alpha != 1.0 && alpha != -1.0) return set_error(OZK_ERR_ARG, "alpha must be +1 or -1");
+  if (!workspace || ((uintptr_t)workspace & 255))
+    return set_error(OZK_ERR_ARG, "the int8 GEMM needs a 256-byte aligned workspace");
+  if (ws_bytes < cur_state_bytes())
+    return set_error(OZK_ERR_WORKSPACE, "workspace %zu bytes < %zu needed", ws_bytes,
+                     cur_state_bytes());
+  return launch_slice_gemm_ex(SA, eA, nA, SB, eB, nB, N, M, k_pad, pair_a, pair_b, n_pairs,
+                              OZK_ACC_FIXED, symmetric, alpha, beta, Cin, ldcin, C, ldc, nullptr,
+                              (double*)workspace, ws_bytes, rho, status_dev, true, skip_if_dev, 0,
+                              (cudaStream_t)stream);
+}
+
 int ozk_accumulate_2sum(const float* products, const int32_t* eA, const int32_t* eB, int64_t N,
                         int64_t M, int n_hi, int n_lo, float* C_hi, float* C_lo, double* C,
                         int64_t ldc, void* stream) {
@@ -385,6 +510,9 @@ int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, d
   if ((rc = ws.acquire(workspace, workspace ? ws_bytes : need, need, s))) return rc;
   Workspace w = layout(ws.ptr, N, K, M, nS, prod ? np : 0, M * K,
                        with_state ? cur_state_bytes() : 0);
+  if (acc_mode == OZK_ACC_FIXED)
+    return matmul_fixed(A, lda, B, ldb, C, ldc, N, K, M, rho, n_hi, n_lo, pa, pb, np, w, status_dev,
+                        s);
   if ((rc = launch_extract_rows(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
     return rc;
   if ((rc = launch_extract_cols(B, ldb, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, w.BT,
@@ -476,6 +604,25 @@ int ozk_gram_f64(const double* A, int64_t lda, double* G, int64_t ldg, int64_t N
   ScopedWs ws;
   if ((rc = ws.acquire(workspace, workspace ? ws_bytes : need, need, s))) return rc;
   Workspace w = layout(ws.ptr, K, N, 0, nS, 0, K * N, sb);
+  const int64_t k8 = round_up(N, kS8KB);
+  if (s8_enabled() && slice_gemm_s8_eligible(K, K, k8, OZK_ACC_FIXED, rho, w.state_bytes)) {
+    // int8 pass, then the gated BF16 recomputation from the transposed copy
+    cudaError_t e = cudaMemsetAsync(w.gate, 0, sizeof(int32_t), s);
+    if (e != cudaSuccess) return set_cuda_error("cudaMemsetAsync(gate)", e);
+    if ((rc = launch_extract_cols_s8(A, lda, N, K, rho, n_hi, n_lo, (int8_t*)w.SA, k8, w.eA,
+                                     status_dev, w.gate, w.BT, s)))
+      return rc;
+    if ((rc = launch_slice_gemm_ex(w.SA, w.eA, nS, w.SA, w.eA, nS, K, K, k8, pa, pb, np,
+                                   OZK_ACC_FIXED, 1, 1.0, 0.0, nullptr, 0, G, ldg, nullptr, w.state,
+                                   w.state_bytes, rho, status_dev, true, w.gate, 0, s)))
+      return rc;
+    if ((rc = launch_extract_rows_gated(w.BT, N, K, N, rho, n_hi, n_lo, w.SA, k_pad, w.eA,
+                                        status_dev, w.gate, s)))
+      return rc;
+    return launch_slice_gemm_ex(w.SA, w.eA, nS, w.SA, w.eA, nS, K, K, k_pad, pa, pb, np,
+                                OZK_ACC_FIXED, 1, 1.0, 0.0, nullptr, 0, G, ldg, nullptr, w.state,
+                                w.state_bytes, rho, status_dev, false, w.gate, 1, s);
+  }
   if ((rc = launch_extract_cols(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, w.BT,
                                 s)))
     return rc;
@@ -556,6 +703,23 @@ const char* ozk_strerror(int status) {
 int ozk_last_error_detail(char* buf, size_t len) {
   if (!buf || !len) return OZK_ERR_ARG;
   snprintf(buf, len, "%s", t_detail);
+  return OZK_OK;
+}
+
+int ozk_set_l2_persisting(size_t bytes, size_t* previous) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_cuda_error("cudaGetDevice", e);
+  size_t prev = 0;
+  if ((e = cudaDeviceGetLimit(&prev, cudaLimitPersistingL2CacheSize)) != cudaSuccess)
+    return set_cuda_error("cudaDeviceGetLimit(persisting L2)", e);
+  int mx = 0;
+  if ((e = cudaDeviceGetAttribute(&mx, cudaDevAttrMaxPersistingL2CacheSize, dev)) != cudaSuccess)
+    return set_cuda_error("cudaDeviceGetAttribute(max persisting L2)", e);
+  if (bytes > (size_t)mx) bytes = (size_t)mx;
+  if ((e = cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, bytes)) != cudaSuccess)
+    return set_cuda_error("cudaDeviceSetLimit(persisting L2)", e);
+  if (previous) *previous = prev;
   return OZK_OK;
 }
 

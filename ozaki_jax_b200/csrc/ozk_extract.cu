@@ -176,14 +176,31 @@ __global__ void __launch_bounds__(NT) k_extract_rows(const double* __restrict__ 
 // kbase + 2*(p*256 + tid) + {0,1}, p < EPT/2, so the loads are 16-byte vectors
 // and the slice stores 4-byte words, both coalesced.  Line maxima are shared
 // across the cluster through distributed shared memory.
+//
+// S8 = true writes each slice as int8 codes q = slice * 2^(24 - rho) instead
+// of BF16 bits: every slice is an integer multiple of 2^(rho - 24) of
+// magnitude <= 2^(25 - rho), so for rho >= 19 the code is exact and |q| <= 64.
+// A value that is not (non-finite slices of out-of-range lines) sets
+// *s8_fail; the caller then recomputes with BF16 slices.  With `gate`
+// non-NULL the kernel runs only when *gate != 0 (the BF16 recomputation).
 constexpr int kRegNT = 256;
 
-template <int EPT, int CL>
+__device__ __forceinline__ uint32_t s8_code(float v, float inv, float scale, bool& bad) {
+  const float q = __fmul_rn(__fmul_rn(v, inv), scale);
+  const int iq = __float2int_rn(q);
+  if (!(fabsf(q) <= 127.0f) || (float)iq != q) bad = true;
+  return (uint32_t)(uint8_t)(int8_t)iq;
+}
+
+template <int EPT, int CL, bool S8>
 __global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
     const double* __restrict__ X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
-    int n_lo, uint16_t* __restrict__ slices, int64_t k_pad, int32_t* __restrict__ exps,
-    int32_t* status, int vec) {
+    int n_lo, void* __restrict__ slices_v, int64_t k_pad, int32_t* __restrict__ exps,
+    int32_t* status, int vec, int32_t* s8_fail, const int32_t* gate) {
   static_assert(EPT % 2 == 0, "EPT must be even");
+  if (gate && *(volatile const int32_t*)gate == 0) return;  // uniform over the grid
+  const float s8_scale = pow2f(24 - rho);
+  bool s8_bad = false;
   __shared__ float s_part[2][2][kRegNT / 32];  // [parity][hi, lo][warp]
   __shared__ float s_cta[2][2];                // [parity][hi, lo] CTA maxima for the cluster
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -258,35 +275,40 @@ __global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
         if (do_hi) exps[(int64_t)t * rows + row] = ch;
         if (do_lo) exps[(int64_t)(n_hi + t) * rows + row] = cl;
       }
-      uint16_t* out_h = slices + (int64_t)t * slice_stride + row * k_pad;
-      uint16_t* out_l = slices + (int64_t)(n_hi + t) * slice_stride + row * k_pad;
+      // Element offsets of this row in the hi and lo slices (BF16: 2 bytes,
+      // S8: 1 byte per element).
+      const int64_t off_h = (int64_t)t * slice_stride + row * k_pad;
+      const int64_t off_l = (int64_t)(n_hi + t) * slice_stride + row * k_pad;
 #pragma unroll
       for (int p = 0; p < EPT / 2; ++p) {
         const int64_t k = kbase + 2 * ((int64_t)p * kRegNT + tid);
-        if (do_hi) {
+#pragma unroll
+        for (int side = 0; side < 2; ++side) {
+          if (side == 0 ? !do_hi : !do_lo) continue;
+          const float sg = side == 0 ? sh : sl, iv = side == 0 ? ih : il;
+          const int zz = side == 0 ? zh : zl;
           uint32_t w = 0;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            float& r = rh[2 * p + h];
-            float v = zh ? 0.0f : __fsub_rn(__fadd_rn(r, sh), sh);
+            float& r = side == 0 ? rh[2 * p + h] : rl[2 * p + h];
+            float v = zz ? 0.0f : __fsub_rn(__fadd_rn(r, sg), sg);
             r = __fsub_rn(r, v);
-            if (k + h < K) w |= (uint32_t)bf16_bits_exact(__fmul_rn(v, ih)) << (16 * h);
+            if (k + h < K) {
+              if constexpr (S8) w |= s8_code(v, iv, s8_scale, s8_bad) << (8 * h);
+              else w |= (uint32_t)bf16_bits_exact(__fmul_rn(v, iv)) << (16 * h);
+            }
           }
-          if (k < k_pad) *reinterpret_cast<uint32_t*>(out_h + k) = w;
-        }
-        if (do_lo) {
-          uint32_t w = 0;
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float& r = rl[2 * p + h];
-            float v = zl ? 0.0f : __fsub_rn(__fadd_rn(r, sl), sl);
-            r = __fsub_rn(r, v);
-            if (k + h < K) w |= (uint32_t)bf16_bits_exact(__fmul_rn(v, il)) << (16 * h);
+          const int64_t off = (side == 0 ? off_h : off_l) + k;
+          if (k < k_pad) {
+            if constexpr (S8) reinterpret_cast<uint16_t*>(static_cast<int8_t*>(slices_v) + off)[0] = (uint16_t)w;
+            else *reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(slices_v) + off) = w;
           }
-          if (k < k_pad) *reinterpret_cast<uint32_t*>(out_l + k) = w;
         }
       }
     }
+  }
+  if constexpr (S8) {
+    if (s8_bad) *s8_fail = 1;
   }
   if constexpr (CL > 1) cluster_sync();  // peers may still read this CTA's s_cta
 }
@@ -630,10 +652,11 @@ int upload_log2_table(int dev) {
   return OZK_OK;
 }
 
-template <int EPT, int CL>
+template <int EPT, int CL, bool S8 = false>
 static int launch_rows_reg(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
-                           int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps,
-                           int32_t* status, int dev, cudaStream_t stream) {
+                           int n_lo, void* slices, int64_t k_pad, int32_t* exps,
+                           int32_t* status, int dev, cudaStream_t stream,
+                           int32_t* s8_fail = nullptr, const int32_t* gate = nullptr) {
   const int vec = (((uintptr_t)X & 15) == 0) && (ldx % 2 == 0);
   // Enough lines in flight per SM to cover the reduction latencies.
   int64_t per_sm = EPT <= 8 ? 8 : (EPT <= 16 ? 6 : 3);
@@ -651,15 +674,45 @@ static int launch_rows_reg(const double* X, int64_t ldx, int64_t rows, int64_t K
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_extract_rows_reg<EPT, CL>, X, ldx, rows, K, rho, n_hi,
-                                     n_lo, slices, k_pad, exps, status, vec);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_extract_rows_reg<EPT, CL, S8>, X, ldx, rows, K, rho,
+                                     n_hi, n_lo, slices, k_pad, exps, status, vec, s8_fail, gate);
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows_reg launch", e);
+}
+
+int launch_extract_rows_s8(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                           int n_hi, int n_lo, int8_t* slices, int64_t k_pad, int32_t* exps,
+                           int32_t* status, int32_t* s8_fail, cudaStream_t stream) {
+  if (rows == 0) return OZK_OK;
+  if (rho < kS8MinRho || k_pad % kS8KB || k_pad > 65536)
+    return set_error(OZK_ERR_UNSUPPORTED, "int8 slices need rho >= %d and k_pad <= 65536, a multiple of %d",
+                     kS8MinRho, kS8KB);
+  if (!s8_fail) return set_error(OZK_ERR_ARG, "s8_fail is NULL");
+  int dev;
+  cudaGetDevice(&dev);
+  int rc = upload_log2_table(dev);
+  if (rc) return rc;
+  // rho >= 19 means K > 4096, so 8192-column CTAs (and clusters for longer lines)
+  if (k_pad <= 8192)
+    return launch_rows_reg<32, 1, true>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, s8_fail);
+  if (k_pad <= 16384)
+    return launch_rows_reg<32, 2, true>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, s8_fail);
+  if (k_pad <= 32768)
+    return launch_rows_reg<32, 4, true>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, s8_fail);
+  return launch_rows_reg<32, 8, true>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, s8_fail);
 }
 
 int launch_extract_rows(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
                         cudaStream_t stream) {
+  return launch_extract_rows_gated(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status,
+                                   nullptr, stream);
+}
+
+int launch_extract_rows_gated(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                              int n_hi, int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                              int32_t* status, const int32_t* gate, cudaStream_t stream) {
   if (rows == 0) return OZK_OK;
+  if (gate && k_pad > 65536) return set_error(OZK_ERR_UNSUPPORTED, "gated extraction needs k_pad <= 65536");
   int dev;
   cudaGetDevice(&dev);
   int rc = upload_log2_table(dev);
@@ -667,21 +720,21 @@ int launch_extract_rows(const double* X, int64_t ldx, int64_t rows, int64_t K, i
   // Register-resident path: one CTA covers 256*EPT columns, a cluster of up to
   // 8 CTAs covers k_pad <= 65536.
   if (k_pad <= 512)
-    return launch_rows_reg<2, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+    return launch_rows_reg<2, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, nullptr, gate);
   if (k_pad <= 1024)
-    return launch_rows_reg<4, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+    return launch_rows_reg<4, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, nullptr, gate);
   if (k_pad <= 2048)
-    return launch_rows_reg<8, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+    return launch_rows_reg<8, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, nullptr, gate);
   if (k_pad <= 4096)
-    return launch_rows_reg<16, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+    return launch_rows_reg<16, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, nullptr, gate);
   if (k_pad <= 8192)
-    return launch_rows_reg<32, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+    return launch_rows_reg<32, 1>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, nullptr, gate);
   if (k_pad <= 16384)
-    return launch_rows_reg<32, 2>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+    return launch_rows_reg<32, 2>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, nullptr, gate);
   if (k_pad <= 32768)
-    return launch_rows_reg<32, 4>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+    return launch_rows_reg<32, 4>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, nullptr, gate);
   if (k_pad <= 65536)
-    return launch_rows_reg<32, 8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream);
+    return launch_rows_reg<32, 8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, nullptr, gate);
   // Longer lines: multi-pass kernel (passes 2.. re-read the line from L2).
   int sms = device_sm_count(dev);
   int64_t grid = rows < sms * 2 ? rows : sms * 2;
@@ -731,6 +784,18 @@ int launch_extract_cols(const double* X, int64_t ldx, int64_t K, int64_t cols, i
                                                             slices, k_pad, exps, status);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_cols launch", e);
+}
+
+int launch_extract_cols_s8(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho,
+                           int n_hi, int n_lo, int8_t* slices, int64_t k_pad, int32_t* exps,
+                           int32_t* status, int32_t* s8_fail, double* scratch,
+                           cudaStream_t stream) {
+  if (cols == 0) return OZK_OK;
+  if (!scratch) return set_error(OZK_ERR_ARG, "int8 column extraction needs the transpose scratch");
+  int rc = launch_transpose_f64(X, ldx, K, cols, scratch, stream);
+  if (rc) return rc;
+  return launch_extract_rows_s8(scratch, K, cols, K, rho, n_hi, n_lo, slices, k_pad, exps, status,
+                                s8_fail, stream);
 }
 
 int launch_extract_rows64(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int ns,

@@ -68,6 +68,8 @@ struct GemmArgs {
   int fix_off;                // -150 - G + kFixFrac, G = product-grid exponent 2 (rho - 24)
   int fix_scale;              // G - kFixFrac: output = sum * 2^(eA0 + eB0 + fix_scale)
   int prefetch;               // L2 prefetch distance in stages (0 = off)
+  const int32_t* gate;        // if set, the kernel runs only when (*gate != 0) == gate_want
+  int gate_want;
 };
 
 // PAIR = false: one CTA per output tile of 128 x BN.
@@ -130,10 +132,16 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& tm, i
 // shares a pipe with the tensor cores on this part).
 constexpr int kFixFrac = 36;
 
+// A non-finite product (from non-finite slices of out-of-range inputs, where
+// the reference's sums are NaN) marks the element with this value, which a
+// real sum never reaches (|terms| < 2^62); it stays set and becomes NaN.
+constexpr long long kFixNaN = (long long)0x8000000000000000ull;
+
 // Term of the FP32 product bits u, t_off = (ea - eA0) + (eb - eB0) + fix_off:
 // round(P * 2^(ea + eb) / unit).
 __device__ __forceinline__ long long fixed_term(uint32_t u, int t_off) {
   const uint32_t ex = (u >> 23) & 0xFFu;
+  if (ex == 0xFFu) return kFixNaN;
   const uint32_t m = (u & 0x7FFFFFu) | (ex ? 0x800000u : 0u);  // products are 0 or normal
   const int T = (int)ex + t_off;
   const int L = min(max(T, 0), 40);
@@ -160,6 +168,24 @@ __device__ __forceinline__ double scaled_term(uint32_t u, int e, uint32_t sign_f
   return (v * pow2d(e / 2)) * pow2d(e - e / 2);
 }
 
+// The same term from an exact int32 product P of int8 slice codes (the
+// product in units of the product grid): round(P * 2^T), half away from zero,
+// T = (ea - eA0) + (eb - eB0) + kFixFrac.  It equals fixed_term of the FP32
+// product of the corresponding BF16 slices bit for bit (the same real number,
+// rounded the same way).
+__device__ __forceinline__ long long fixed_term_s32(int32_t P, int T) {
+  const unsigned long long a = (unsigned long long)(P < 0 ? -(long long)P : (long long)P);
+  unsigned long long v;
+  if (T >= 0) {
+    v = a << min(T, 40);
+  } else {
+    const int R = min(-T, 40);
+    v = (a + (1ull << (R - 1))) >> R;
+  }
+  const long long sg = (long long)(P >> 31);  // 0 or -1
+  return ((long long)v ^ sg) - sg;
+}
+
 // The FP64 value of a fixed-point sum: acc * 2^e, exact scaling.
 __device__ __forceinline__ double fixed_value(long long acc, int e) {
   const double v = __ll2double_rn(acc);
@@ -167,11 +193,19 @@ __device__ __forceinline__ double fixed_value(long long acc, int e) {
   return (v * pow2d(e / 2)) * pow2d(e - e / 2);
 }
 
-template <int BN, bool PAIR>
+// S8 = true: int8 slice codes and kind::i8 MMAs into exact int32 accumulators
+// (OZK_ACC_FIXED only, CTA pairs only); a pipeline stage then holds 128 K
+// elements, the same bytes as 64 BF16 ones.
+template <int BN, bool PAIR, bool S8>
 __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
     k_slice_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
                  const __grid_constant__ PairList pairs, const __grid_constant__ GemmArgs g) {
+  static_assert(!S8 || PAIR, "int8 slices run on CTA pairs");
   using Cfg = GemmCfg<BN, PAIR>;
+  constexpr int KBE = S8 ? kS8KB : OZK_KB;  // K elements per stage
+  // Device-side choice between the int8 pass and its BF16 recomputation: every
+  // CTA reads the same word, so the whole grid leaves before any setup.
+  if (g.gate && ((*(volatile const int32_t*)g.gate != 0) != (g.gate_want != 0))) return;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int CH = Cfg::CH;
   extern __shared__ uint8_t smem_raw[];
@@ -243,8 +277,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
                 ++pp;
               }
               if (pp < npairs && pk < g.num_kb) {
-                tma_prefetch_3d(&mapA, pk * OZK_KB, arow, pairs.a[pp]);
-                tma_prefetch_3d(&mapB, pk * OZK_KB, brow, pairs.b[pp]);
+                tma_prefetch_3d(&mapA, pk * KBE, arow, pairs.a[pp]);
+                tma_prefetch_3d(&mapB, pk * KBE, brow, pairs.b[pp]);
               }
             }
             long long c0 = clock64();
@@ -256,12 +290,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
             if constexpr (PAIR) {
               if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
               const uint32_t fb = mapa_u32(&full[s], 0);
-              tma_load_3d_pair(sA + s * Cfg::A_BYTES, &mapA, fb, kb * OZK_KB, arow, a);
-              tma_load_3d_pair(sB + s * Cfg::B_BYTES, &mapB, fb, kb * OZK_KB, brow, b);
+              tma_load_3d_pair(sA + s * Cfg::A_BYTES, &mapA, fb, kb * KBE, arow, a);
+              tma_load_3d_pair(sB + s * Cfg::B_BYTES, &mapB, fb, kb * KBE, brow, b);
             } else {
               mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-              tma_load_3d(sA + s * Cfg::A_BYTES, &mapA, &full[s], kb * OZK_KB, arow, a);
-              tma_load_3d(sB + s * Cfg::B_BYTES, &mapB, &full[s], kb * OZK_KB, brow, b);
+              tma_load_3d(sA + s * Cfg::A_BYTES, &mapA, &full[s], kb * KBE, arow, a);
+              tma_load_3d(sB + s * Cfg::B_BYTES, &mapB, &full[s], kb * KBE, brow, b);
             }
             ++it;
           }
@@ -280,10 +314,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(Cfg::TILE_M, BN);
+      constexpr uint32_t idesc = S8 ? umma_idesc_s8(Cfg::TILE_M, BN) : umma_idesc_bf16(Cfg::TILE_M, BN);
       uint32_t it = 0, acc_it = 0;
       bool ok = true;
-      long long w_acc = 0, w_full = 0, t_start = clock64();
+      long long w_acc = 0, w_full = 0, w_head = 0, t_start = clock64();
       for (int t = unit; ok && t < g.num_tiles; t += n_units) {
         for (int p = 0; ok && p < npairs; ++p) {
           const uint32_t buf = acc_it & 1, aph = (acc_it >> 1) & 1;
@@ -302,7 +336,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
               ok = false;
               break;
             }
-            w_full += clock64() - c1;
+            {
+              const long long wf = clock64() - c1;
+              w_full += wf;
+              if (kb < STAGES) w_head += wf;
+            }
             tc_fence_after();
             const uint32_t a0 = smem_u32(sA + s * Cfg::A_BYTES);
             const uint32_t b0 = smem_u32(sB + s * Cfg::B_BYTES);
@@ -310,7 +348,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
             for (int kk = 0; kk < OZK_KB / 16; ++kk) {
               const uint64_t da = umma_desc_sw128(a0 + kk * 32);
               const uint64_t db = umma_desc_sw128(b0 + kk * 32);
-              if constexpr (PAIR) umma_bf16_pair(d, da, db, idesc, (kb | kk) != 0);
+              if constexpr (S8) umma_s8_pair(d, da, db, idesc, (kb | kk) != 0);
+              else if constexpr (PAIR) umma_bf16_pair(d, da, db, idesc, (kb | kk) != 0);
               else umma_bf16(d, da, db, idesc, (kb | kk) != 0);
             }
             if constexpr (PAIR) umma_commit_pair(&empty[s], 0x3);
@@ -332,6 +371,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
         st[0] = (unsigned long long)w_acc;
         st[1] = (unsigned long long)w_full;
         st[3] = (unsigned long long)(clock64() - t_start);
+        st[7] = (unsigned long long)w_head;
       }
     }
     __syncwarp();
@@ -424,14 +464,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
           }
           if (g.fixed) {
             // ---- int64 fixed-point sums (integer pipes only until the last pair)
-            const int ta = ea - eA0 + g.fix_off;
+            const int ta = ea - eA0 + (S8 ? kFixFrac : g.fix_off);
 #pragma unroll
             for (int j = 0; j < CH; ++j) {
               const int db = b == 0 ? 0 : s_eB[b * BN + c0 + j];  // eb - eB0
-              long long acc = fixed_term(P[j], ta + db);
+              long long acc;
+              if constexpr (S8) acc = fixed_term_s32((int32_t)P[j], ta + db);
+              else acc = fixed_term(P[j], ta + db);
               if (!first) {
-                if constexpr (Cfg::GSTATE) acc += __double_as_longlong(S[j]);
-                else acc += (long long)(((unsigned long long)H[j] << 32) | L[j]);
+                long long prev;
+                if constexpr (Cfg::GSTATE) prev = __double_as_longlong(S[j]);
+                else prev = (long long)(((unsigned long long)H[j] << 32) | L[j]);
+                if constexpr (S8) acc += prev;  // int8 codes are finite by construction
+                else acc = (acc == kFixNaN || prev == kFixNaN) ? kFixNaN : acc + prev;
               }
               if (!last) {
                 if constexpr (Cfg::GSTATE) {
@@ -441,7 +486,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
                   H[j] = (uint32_t)((unsigned long long)acc >> 32);
                 }
               } else {
-                double v = fixed_value(acc, eA0 + s_eB[c0 + j] + g.fix_scale);
+                double v = acc == kFixNaN ? __longlong_as_double(0x7ff8000000000000ll)
+                                          : fixed_value(acc, eA0 + s_eB[c0 + j] + g.fix_scale);
                 v = g.alpha * v;
                 if (g.beta != 0.0 && rvalid && col0 + c0 + j < g.M)
                   v = fma(g.beta, g.Cin[row * g.ldcin + col0 + c0 + j], v);
@@ -597,6 +643,19 @@ static int prefetch_distance() {
   return v;
 }
 
+// Tile rows per raster group (OZK_GEMM_GROUP_M, default 8): consecutive tiles
+// walk down a group of this many tile rows before moving right, so the tiles
+// in flight at once share few A and B panels in L2.
+static int group_m_rows() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("OZK_GEMM_GROUP_M");
+    v = s ? atoi(s) : 8;
+    if (v < 1) v = 8;
+  }
+  return v;
+}
+
 // CTA-pair tiles are the default for wide outputs; OZK_GEMM_PAIR=0 selects
 // single-CTA tiles (kept for comparison and as a fallback).
 static bool pair_mode_enabled() {
@@ -620,28 +679,31 @@ static int get_encode_fn() {
   return OZK_OK;
 }
 
-// Tensor map over a [depth][rows][k_pad] BF16 slice stack, box 64 x box_rows.
-static int make_slice_map(CUtensorMap* map, const uint16_t* base, int64_t k_pad, int64_t rows,
-                          int depth, int box_rows) {
+// Tensor map over a [depth][rows][k_pad] slice stack (BF16, or int8 codes
+// with s8), box of 128 bytes x box_rows.
+static int make_slice_map(CUtensorMap* map, const void* base, int64_t k_pad, int64_t rows,
+                          int depth, int box_rows, bool s8) {
   if (((uintptr_t)base & 15) != 0) return set_error(OZK_ERR_ARG, "slice buffer not 16-byte aligned");
+  const int64_t esz = s8 ? 1 : 2;
   cuuint64_t dims[3] = {(cuuint64_t)k_pad, (cuuint64_t)rows, (cuuint64_t)depth};
-  cuuint64_t strides[2] = {(cuuint64_t)(k_pad * 2), (cuuint64_t)(k_pad * 2 * rows)};
-  cuuint32_t box[3] = {OZK_KB, (cuuint32_t)box_rows, 1};
+  cuuint64_t strides[2] = {(cuuint64_t)(k_pad * esz), (cuuint64_t)(k_pad * esz * rows)};
+  cuuint32_t box[3] = {(cuuint32_t)(s8 ? kS8KB : OZK_KB), (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, (void*)base, dims, strides, box,
+  CUresult r = g_encode(map, s8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        3, (void*)base, dims, strides, box,
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(OZK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return OZK_OK;
 }
 
-template <int BN, bool PAIR>
+template <int BN, bool PAIR, bool S8 = false>
 static int launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const PairList& pl,
                      const GemmArgs& ga, int dev, cudaStream_t stream) {
   using Cfg = GemmCfg<BN, PAIR>;
   static int configured[64] = {0};
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_slice_gemm<BN, PAIR>,
+    cudaError_t e = cudaFuncSetAttribute(k_slice_gemm<BN, PAIR, S8>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k_slice_gemm)", e);
@@ -671,7 +733,7 @@ static int launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const PairLis
     g_stats_ctas[dev] = units * per;
     g_stats_last_dev = dev;
   }
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_slice_gemm<BN, PAIR>, ma, mb, pl, gl);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_slice_gemm<BN, PAIR, S8>, ma, mb, pl, gl);
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_slice_gemm launch", e);
 }
 
@@ -685,9 +747,34 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
                       int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
                       double* C, int64_t ldc, float* products, double* state, size_t state_bytes,
                       int rho, int32_t* status, cudaStream_t stream) {
+  return launch_slice_gemm_ex(SA, eA, nA, SB, eB, nB, N, M, k_pad, pair_a, pair_b, n_pairs, mode,
+                              symmetric, alpha, beta, Cin, ldcin, C, ldc, products, state,
+                              state_bytes, rho, status, false, nullptr, 0, stream);
+}
+
+bool slice_gemm_s8_eligible(int64_t N, int64_t M, int64_t k_pad, int mode, int rho,
+                            size_t state_bytes) {
+  int dev;
+  cudaGetDevice(&dev);
+  return mode == OZK_ACC_FIXED && rho >= kS8MinRho && N >= 256 && M >= 256 && k_pad > 0 &&
+         k_pad % kS8KB == 0 && k_pad <= 65536 && state_bytes >= gemm_state_bytes(dev) &&
+         pair_mode_enabled();
+}
+
+int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* SB,
+                         const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
+                         const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
+                         int symmetric, double alpha, double beta, const double* Cin,
+                         int64_t ldcin, double* C, int64_t ldc, float* products, double* state,
+                         size_t state_bytes, int rho, int32_t* status, bool s8,
+                         const int32_t* gate, int gate_want, cudaStream_t stream) {
   if (N == 0 || M == 0) return OZK_OK;
   if (n_pairs < 1 || n_pairs > OZK_MAX_PAIRS) return set_error(OZK_ERR_ARG, "n_pairs out of range");
   if (k_pad <= 0 || k_pad % OZK_KB) return set_error(OZK_ERR_ARG, "k_pad must be a positive multiple of 64");
+  if (s8 && !slice_gemm_s8_eligible(N, M, k_pad, mode, rho, state_bytes))
+    return set_error(OZK_ERR_UNSUPPORTED,
+                     "int8 slices need OZK_ACC_FIXED, rho >= %d, N and M >= 256, k_pad a multiple of "
+                     "%d up to 65536 and the GEMM state scratch", kS8MinRho, kS8KB);
   if (nA < 1 || nA > OZK_MAX_SLICES || nB < 1 || nB > OZK_MAX_SLICES)
     return set_error(OZK_ERR_ARG, "slice counts out of range");
   for (int p = 0; p < n_pairs; ++p)
@@ -711,15 +798,15 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
   // scratch) for large FP64 outputs; 256 x 128 on CTA pairs (sums in TMEM)
   // when no scratch is given; narrow single-CTA tiles for narrow outputs
   // (e.g. residual right-hand sides).
-  const bool wide = mode != OZK_ACC_PRODUCTS && N >= 256 && M >= 256 && state &&
-                    state_bytes >= gemm_state_bytes(dev) && pair_mode_enabled();
+  const bool wide = s8 || (mode != OZK_ACC_PRODUCTS && N >= 256 && M >= 256 && state &&
+                          state_bytes >= gemm_state_bytes(dev) && pair_mode_enabled());
   const int BN = wide ? 256 : (M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128)));
   const int bn = (symmetric && !wide) ? 128 : BN;
   const bool pair = wide || (!symmetric && bn == 128 && pair_mode_enabled());
   const int tile_m = pair ? 2 * kBM : kBM;
   CUtensorMap ma, mb;
-  if ((rc = make_slice_map(&ma, SA, k_pad, N, nA, kBM))) return rc;
-  if ((rc = make_slice_map(&mb, SB, k_pad, M, nB, pair ? bn / 2 : bn))) return rc;
+  if ((rc = make_slice_map(&ma, SA, k_pad, N, nA, kBM, s8))) return rc;
+  if ((rc = make_slice_map(&mb, SB, k_pad, M, nB, pair ? bn / 2 : bn, s8))) return rc;
 
   PairList pl;
   memset(&pl, 0, sizeof(pl));
@@ -734,12 +821,12 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
   ga.eB = eB;
   ga.N = N;
   ga.M = M;
-  ga.num_kb = (int)(k_pad / OZK_KB);
+  ga.num_kb = (int)(k_pad / (s8 ? kS8KB : OZK_KB));
   ga.nB = nB;
   ga.tiles_m = (int)((N + tile_m - 1) / tile_m);
   ga.tiles_n = (int)((M + bn - 1) / bn);
   ga.num_tiles = symmetric ? ga.tiles_m * (ga.tiles_m + 1) / 2 : ga.tiles_m * ga.tiles_n;
-  ga.group_m = 8;
+  ga.group_m = group_m_rows();
   ga.mode = mode;
   ga.symmetric = symmetric;
   ga.alpha = alpha;
@@ -757,6 +844,9 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
   ga.fix_off = -150 - 2 * (rho - 24) + kFixFrac;
   ga.fix_scale = 2 * (rho - 24) - kFixFrac;
   ga.prefetch = prefetch_distance();
+  ga.gate = gate;
+  ga.gate_want = gate_want;
+  if (s8) return launch_bn<256, true, true>(ma, mb, pl, ga, dev, stream);
   if (wide) return launch_bn<256, true>(ma, mb, pl, ga, dev, stream);
   switch (bn) {
     case 16: return launch_bn<16, false>(ma, mb, pl, ga, dev, stream);

@@ -18,13 +18,36 @@ int set_error(int code, const char* fmt, ...);
 int set_cuda_error(const char* what, cudaError_t e);
 
 int device_sm_count(int dev);
+// BF16 -> FP32 exact inner-product bound K * (2^bits - 1)^2 < 2^24; returns
+// OZK_ERR_UNSAFE (with the detail text) when violated.
+int check_bound(int64_t K, int bits);
 uint64_t wait_budget_ns();
 
 inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
+// int8 slices: exact for rho >= 19 (|code| <= 64); a pipeline stage holds 128
+// int8 K-elements (the same 128 bytes per row as 64 BF16 elements).
+constexpr int kS8MinRho = 19;
+constexpr int kS8KB = 128;
+
 int launch_extract_rows(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
                         int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
                         cudaStream_t stream);
+// With gate non-NULL the kernels do nothing unless *gate != 0 (device-side
+// recomputation after a failed int8 extraction); needs k_pad <= 65536.
+int launch_extract_rows_gated(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                              int n_hi, int n_lo, uint16_t* slices, int64_t k_pad, int32_t* exps,
+                              int32_t* status, const int32_t* gate, cudaStream_t stream);
+// int8 slice codes (slice * 2^(24 - rho)), [n_hi+n_lo][rows][k_pad] int8; needs
+// rho >= kS8MinRho and k_pad a multiple of kS8KB, <= 65536.  Sets *s8_fail = 1
+// when a slice value has no exact code (the caller then recomputes in BF16).
+int launch_extract_rows_s8(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                           int n_hi, int n_lo, int8_t* slices, int64_t k_pad, int32_t* exps,
+                           int32_t* status, int32_t* s8_fail, cudaStream_t stream);
+int launch_extract_cols_s8(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho,
+                           int n_hi, int n_lo, int8_t* slices, int64_t k_pad, int32_t* exps,
+                           int32_t* status, int32_t* s8_fail, double* scratch,
+                           cudaStream_t stream);
 // scratch: cols x K FP64 buffer for the transposed fast path (NULL selects the
 // multi-pass column kernel).
 int launch_extract_cols(const double* X, int64_t ldx, int64_t K, int64_t cols, int rho, int n_hi,
@@ -44,6 +67,23 @@ int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint1
                       int symmetric, double alpha, double beta, const double* Cin, int64_t ldcin,
                       double* C, int64_t ldc, float* products, double* state, size_t state_bytes,
                       int rho, int32_t* status, cudaStream_t stream);
+// The same with the slice type and a device-side gate: s8 selects int8 slice
+// codes (layout [n][rows][k_pad] int8, k_pad a multiple of kS8KB) and the
+// kind::i8 kernel; with gate non-NULL the kernel does nothing unless
+// (*gate != 0) == gate_want.
+int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* SB,
+                         const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
+                         const uint8_t* pair_a, const uint8_t* pair_b, int n_pairs, int mode,
+                         int symmetric, double alpha, double beta, const double* Cin,
+                         int64_t ldcin, double* C, int64_t ldc, float* products, double* state,
+                         size_t state_bytes, int rho, int32_t* status, bool s8,
+                         const int32_t* gate, int gate_want, cudaStream_t stream);
+// Whether the int8 GEMM serves this request (fixed-point sums, rho >= 19,
+// 256-wide tiles with the state scratch, k_pad within the extraction limits).
+bool slice_gemm_s8_eligible(int64_t N, int64_t M, int64_t k_pad, int mode, int rho,
+                            size_t state_bytes);
+// int8 slices enabled (OZK_S8=0 in the environment turns them off).
+bool s8_enabled();
 // Bytes of the per-CTA FP64 state scratch the 256-wide GEMM tiles need.
 size_t gemm_state_bytes(int dev);
 // Smallest workspace ozk_matmul_f64 (OZK_ACC_F64) accepts: without the state

@@ -23,6 +23,8 @@ Accumulation of the exact per-pair products (the `accumulation` argument):
                                ondevice result bit for bit.
 """
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -162,8 +164,7 @@ def _ondevice_device(Ad, Bd, n_hi, n_lo, accumulation, rho=None, out=None):
     dev = Ad.device
     C = out if out is not None else torch.empty((N, M), dtype=torch.float64, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    mode = {"ondevice": L.OZK_ACC_PRODUCTS, "host": L.OZK_ACC_F64}.get(accumulation,
-                                                                       L.OZK_ACC_FIXED)
+    mode = _acc_mode(accumulation)
     ws_bytes = lib.ozk_matmul_workspace_bytes(N, K, M, n_hi, n_lo)
     if mode == L.OZK_ACC_PRODUCTS:
         ws_bytes += (n_hi * n_hi + 2 * n_hi * n_lo) * N * M * 4 + 256
@@ -173,6 +174,35 @@ def _ondevice_device(Ad, Bd, n_hi, n_lo, accumulation, rho=None, out=None):
         N, K, M, -1 if rho is None else rho, n_hi, n_lo, mode, ws.data_ptr(), ws_bytes,
         status.data_ptr(), D.stream_handle(dev)))
     return C, status
+
+
+def _acc_mode(accumulation):
+    return {"ondevice": L.OZK_ACC_PRODUCTS, "host": L.OZK_ACC_F64}.get(accumulation,
+                                                                      L.OZK_ACC_FIXED)
+
+
+def _ondevice_hostbuf(A, B, n_hi, n_lo, accumulation, rho, dev):
+    """NumPy in -> NumPy out through ozk_matmul_f64_hostbuf: the library copies
+    A and B in and C out itself, overlapping the copies with the compute.
+    Returns (C as a NumPy array, OZK_FLAG_* bits)."""
+    lib = L.load()
+    Ah = np.ascontiguousarray(A, dtype=np.float64)
+    Bh = np.ascontiguousarray(B, dtype=np.float64)
+    N, K = Ah.shape
+    M = Bh.shape[1]
+    Ch = D.host_empty_f64((N, M))
+    mode = _acc_mode(accumulation)
+    with torch.cuda.device(dev):
+        ws_bytes = lib.ozk_matmul_hostbuf_workspace_bytes(N, K, M, n_hi, n_lo, mode, 0)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        flags = ctypes.c_int32(0)
+        L.check(lib.ozk_matmul_f64_hostbuf(
+            Ah.ctypes.data, K, Bh.ctypes.data, M, Ch.ctypes.data, M, N, K, M, rho, n_hi, n_lo,
+            mode, 0, ws.data_ptr(), ws_bytes, ctypes.byref(flags), D.stream_handle(dev)))
+        del ws
+    if flags.value & L.OZK_FLAG_TIMEOUT:
+        raise L.OzakiError(L.OZK_ERR_TIMEOUT, "a device-side wait exceeded its time budget")
+    return Ch, flags.value
 
 
 def _matmul_ondevice(A, B, safe_mode, accumulation, n_hi, n_lo):
@@ -186,6 +216,13 @@ def _matmul_ondevice(A, B, safe_mode, accumulation, n_hi, n_lo):
     reasons = _bound_reasons(K, bits, "FP32 extraction")
     _validate_safe_mode(safe_mode)
     dev = D.device_of(A, B)
+    if not D.is_device_array(A) and not reasons and N > 0 and M > 0 and K > 0:
+        C, flags = _ondevice_hostbuf(A, B, n_hi, n_lo, accumulation, rho, dev)
+        if not flags:
+            return C
+        if safe_mode == "fallback":
+            return _fallback(D.to_device_f64(A, dev), D.to_device_f64(B, dev))
+        raise ValueError(_PREFIX + "; ".join(_flags_reasons(flags)))
     Ad = D.to_device_f64(A, dev)
     Bd = D.to_device_f64(B, dev)
     if reasons:
@@ -232,4 +269,6 @@ def matmul(A, B, n_slices=8, safe_mode="raise", pipeline="host",
         C = matmul_host(A, B, n_slices, safe_mode)
     else:
         raise ValueError(f"Unknown pipeline={pipeline!r}; expected 'host' or 'ondevice'.")
-    return C if input_is_device else D.to_host_f64(C)
+    if input_is_device or isinstance(C, np.ndarray):
+        return C
+    return D.to_host_f64(C)

@@ -18,6 +18,7 @@
 // below are sized for.
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "ozk_device.cuh"
 #include "ozk_internal.h"
@@ -311,6 +312,191 @@ __global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
     if (s8_bad) *s8_fail = 1;
   }
   if constexpr (CL > 1) cluster_sync();  // peers may still read this CTA's s_cta
+}
+
+// ---------------------------------------------------------------- rows, staged by bulk copies
+
+// Rows of 1024 < K <= 12288 FP64 values (even K, 16-byte aligned rows): a
+// persistent CTA of NT threads walks rows blockIdx.x, += gridDim.x.  A row
+// arrives in shared memory through bulk copies, is moved into registers (EPT
+// columns per thread, in groups of four adjacent columns) and split, and the
+// buffer is refilled with the CTA's next row at once, so its DRAM transfer
+// overlaps the slice passes of this one; several CTAs per SM keep several
+// rows in flight.  Each slice pass also takes the maximum of the new residual
+// for the next pass, so a pass is one block reduction plus one register sweep.
+// Slices are written as 8-byte (BF16) or 4-byte (int8) words, all columns up
+// to k_pad included.
+//
+// int8 codes: with the slice exponent c of a line in [-127, 127 - rho] (and
+// the line finite), t = RN32(r + sigma) lies in [2^(rho+c-1), 2^(rho+c)), a
+// binade whose spacing 2^(rho+c-24) is the grid of v = t - sigma, with
+// |v| <= 2^(c+1).  So the code q = v * 2^(24-rho-c), an integer with
+// |q| <= 2^(25-rho) <= 64, is the difference of the bit patterns of t and
+// sigma.  Lines outside that range (or holding NaN/Inf or values beyond the
+// FP32 range) set *s8_fail instead, once per line.
+constexpr uint32_t kBulkChunk = 16384;  // bytes per bulk copy instruction
+
+template <int NT, int EPT, int MINB, bool S8>
+__global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
+    const double* __restrict__ X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
+    int n_lo, void* __restrict__ slices_v, int64_t k_pad, int32_t* __restrict__ exps,
+    int32_t* status, int32_t* s8_fail, const int32_t* gate, uint64_t budget_ns) {
+  static_assert(EPT % 4 == 0, "EPT must be a multiple of 4");
+  constexpr int NG = EPT / 4;
+  constexpr int NW = NT / 32;
+  if (gate && *(volatile const int32_t*)gate == 0) return;  // uniform over the grid
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ uint64_t s_bar;
+  __shared__ float s_part[2][2][NW];  // [parity][hi, lo][warp]
+  __shared__ int s_abort;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t row_bytes = (uint32_t)(K * 8);
+  const int npass = n_hi > n_lo ? n_hi : n_lo;
+  const int64_t slice_stride = rows * k_pad;
+  const double* xb = reinterpret_cast<const double*>(smem_raw);
+
+  if (tid == 0) {
+    mbar_init(&s_bar, 1);
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int64_t row) {
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(X + row * ldx);
+    mbar_arrive_expect_tx(&s_bar, row_bytes);
+    for (uint32_t off = 0; off < row_bytes; off += kBulkChunk)
+      bulk_load_g2s(smem_raw + off, src + off, min(kBulkChunk, row_bytes - off), &s_bar);
+  };
+  uint32_t issued = 0;  // rows whose copy was issued (thread 0's count)
+  if (tid == 0 && (int64_t)blockIdx.x < rows) {
+    issue(blockIdx.x);
+    ++issued;
+  }
+  uint32_t it = 0, par = 0;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
+    // All threads wait for the row; the decision to go on is taken together,
+    // so no thread can reach a barrier the others have left.
+    const bool got = mbar_wait(&s_bar, it & 1, (volatile int*)&s_abort, status, budget_ns);
+    if (__syncthreads_or(!got)) break;
+    float rh[EPT], rl[EPT];
+    float mh = 0.0f, ml = 0.0f;
+    int32_t flags = 0;
+#pragma unroll
+    for (int q = 0; q < NG; ++q) {
+      const int64_t k = 4 * ((int64_t)q * NT + tid);
+      double x[4] = {0.0, 0.0, 0.0, 0.0};
+      if (k + 3 < K) {
+        const double2 a2 = *reinterpret_cast<const double2*>(xb + k);
+        const double2 b2 = *reinterpret_cast<const double2*>(xb + k + 2);
+        x[0] = a2.x, x[1] = a2.y, x[2] = b2.x, x[3] = b2.y;
+      } else {
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+          if (k + h < K) x[h] = xb[k + h];
+      }
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float& hi = rh[4 * q + h];
+        float& lo = rl[4 * q + h];
+        split_f64(x[h], hi, lo);
+        flags |= check_value(x[h], hi);
+        mh = fmaxf(mh, fabsf(hi));
+        ml = fmaxf(ml, fabsf(lo));
+      }
+    }
+    if (flags) raise_flag(status, flags);
+    // The buffer is free: fetch this CTA's next row while slicing this one.
+    const int line_bad = __syncthreads_or(flags);
+    if (tid == 0) {
+      const int64_t nx = row + (int64_t)gridDim.x;
+      if (nx < rows) {
+        fence_proxy_async_smem();
+        issue(nx);
+        ++issued;
+      }
+    }
+    bool bad = S8 && line_bad;
+    for (int t = 0; t < npass; ++t, par ^= 1) {
+      const bool do_hi = t < n_hi, do_lo = t < n_lo;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
+        ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, o));
+      }
+      if (lane == 0) {
+        s_part[par][0][warp] = mh;
+        s_part[par][1][warp] = ml;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        mh = fmaxf(mh, s_part[par][0][w]);
+        ml = fmaxf(ml, s_part[par][1][w]);
+      }
+      float sh = 0.f, ih = 0.f, sl = 0.f, il = 0.f;
+      int zh = 1, zl = 1, ch = 0, cl = 0;
+      if (do_hi) slice_params(mh, rho, sh, ih, zh, ch);
+      if (do_lo) slice_params(ml, rho, sl, il, zl, cl);
+      if (S8) {
+        if (do_hi && !zh && (ch < -127 || rho + ch > 127)) bad = true;
+        if (do_lo && !zl && (cl < -127 || rho + cl > 127)) bad = true;
+      }
+      if (tid == 0) {
+        if (do_hi) exps[(int64_t)t * rows + row] = ch;
+        if (do_lo) exps[(int64_t)(n_hi + t) * rows + row] = cl;
+      }
+      mh = 0.0f;
+      ml = 0.0f;
+      const int64_t off_h = (int64_t)t * slice_stride + row * k_pad;
+      const int64_t off_l = (int64_t)(n_hi + t) * slice_stride + row * k_pad;
+#pragma unroll
+      for (int q = 0; q < NG; ++q) {
+        const int64_t k = 4 * ((int64_t)q * NT + tid);
+#pragma unroll
+        for (int side = 0; side < 2; ++side) {
+          if (side == 0 ? !do_hi : !do_lo) continue;
+          const float sg = side == 0 ? sh : sl, iv = side == 0 ? ih : il;
+          const int zz = side == 0 ? zh : zl;
+          const uint32_t sg_bits = __float_as_uint(sg);
+          uint32_t w0 = 0, w1 = 0;
+          float mnext = 0.0f;
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            float& r = side == 0 ? rh[4 * q + h] : rl[4 * q + h];
+            const float tt = __fadd_rn(r, sg);
+            const float v = zz ? 0.0f : __fsub_rn(tt, sg);
+            r = __fsub_rn(r, v);
+            mnext = fmaxf(mnext, fabsf(r));
+            if constexpr (S8) {
+              // (columns >= K hold r = 0, so their code is 0)
+              w0 |= ((__float_as_uint(tt) - sg_bits) & 0xFFu) << (8 * h);
+            } else {
+              const uint32_t bits = bf16_bits_exact(__fmul_rn(v, iv));
+              if (h < 2) w0 |= bits << (16 * h);
+              else w1 |= bits << (16 * (h - 2));
+            }
+          }
+          if (side == 0) mh = fmaxf(mh, mnext);
+          else ml = fmaxf(ml, mnext);
+          if (k < k_pad) {
+            const int64_t off = (side == 0 ? off_h : off_l) + k;
+            if constexpr (S8) {
+              *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(slices_v) + off) = w0;
+            } else {
+              *reinterpret_cast<uint2*>(static_cast<uint16_t*>(slices_v) + off) = make_uint2(w0, w1);
+            }
+          }
+        }
+      }
+    }
+    if (S8 && bad && tid == 0) *s8_fail = 1;
+  }
+  // Every issued copy lands before the CTA's shared memory is released.
+  if (tid == 0) {
+    for (uint32_t j = it; j < issued; ++j)
+      mbar_wait(&s_bar, j & 1, nullptr, status, budget_ns);
+  }
+  __syncthreads();
 }
 
 // ---------------------------------------------------------------- transpose
@@ -679,6 +865,65 @@ static int launch_rows_reg(const double* X, int64_t ldx, int64_t rows, int64_t K
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows_reg launch", e);
 }
 
+template <int NT, int EPT, int MINB, bool S8>
+static int launch_rows_bulk(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                            int n_hi, int n_lo, void* slices, int64_t k_pad, int32_t* exps,
+                            int32_t* status, int32_t* s8_fail, const int32_t* gate, int dev,
+                            cudaStream_t stream) {
+  constexpr size_t kMaxSmem = (size_t)EPT * NT * 8;
+  static int configured[64] = {0};
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_extract_rows_bulk<NT, EPT, MINB, S8>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k_extract_rows_bulk)", e);
+    configured[dev] = 1;
+  }
+  const size_t smem = (size_t)round_up(K * 8, 128);
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_extract_rows_bulk<NT, EPT, MINB, S8>,
+                                                    NT, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  int64_t grid = (int64_t)device_sm_count(dev) * per_sm;
+  if (grid > rows) grid = rows;
+  k_extract_rows_bulk<NT, EPT, MINB, S8><<<(unsigned)grid, NT, smem, stream>>>(
+      X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, s8_fail, gate,
+      wait_budget_ns());
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows_bulk launch", e);
+}
+
+// The bulk-staged kernel serves rows of 1024 < K, k_pad <= 12288 with even K
+// and ldx and a 16-byte aligned base (OZK_EXTRACT_BULK=0 turns it off).
+static bool bulk_rows_ok(const double* X, int64_t ldx, int64_t K, int64_t k_pad) {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("OZK_EXTRACT_BULK");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on && K > 1024 && k_pad <= 12288 && K % 2 == 0 && ldx % 2 == 0 &&
+         ((uintptr_t)X & 15) == 0;
+}
+
+template <bool S8>
+static int launch_rows_bulk_any(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                                int n_hi, int n_lo, void* slices, int64_t k_pad, int32_t* exps,
+                                int32_t* status, int32_t* s8_fail, const int32_t* gate, int dev,
+                                cudaStream_t stream) {
+  // 256-thread CTAs, several per SM (each with one row in flight), up to
+  // 8192 columns; 512 threads (one CTA per SM) beyond.
+  if (k_pad <= 2048)
+    return launch_rows_bulk<256, 8, 4, S8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
+                                           status, s8_fail, gate, dev, stream);
+  if (k_pad <= 4096)
+    return launch_rows_bulk<256, 16, 3, S8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
+                                            status, s8_fail, gate, dev, stream);
+  if (k_pad <= 8192)
+    return launch_rows_bulk<256, 32, 2, S8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
+                                            status, s8_fail, gate, dev, stream);
+  return launch_rows_bulk<512, 24, 1, S8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
+                                          status, s8_fail, gate, dev, stream);
+}
+
 int launch_extract_rows_s8(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
                            int n_hi, int n_lo, int8_t* slices, int64_t k_pad, int32_t* exps,
                            int32_t* status, int32_t* s8_fail, cudaStream_t stream) {
@@ -691,6 +936,9 @@ int launch_extract_rows_s8(const double* X, int64_t ldx, int64_t rows, int64_t K
   cudaGetDevice(&dev);
   int rc = upload_log2_table(dev);
   if (rc) return rc;
+  if (bulk_rows_ok(X, ldx, K, k_pad))
+    return launch_rows_bulk_any<true>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
+                                      status, s8_fail, nullptr, dev, stream);
   // rho >= 19 means K > 4096, so 8192-column CTAs (and clusters for longer lines)
   if (k_pad <= 8192)
     return launch_rows_reg<32, 1, true>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, dev, stream, s8_fail);
@@ -717,6 +965,9 @@ int launch_extract_rows_gated(const double* X, int64_t ldx, int64_t rows, int64_
   cudaGetDevice(&dev);
   int rc = upload_log2_table(dev);
   if (rc) return rc;
+  if (bulk_rows_ok(X, ldx, K, k_pad))
+    return launch_rows_bulk_any<false>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
+                                       status, nullptr, gate, dev, stream);
   // Register-resident path: one CTA covers 256*EPT columns, a cluster of up to
   // 8 CTAs covers k_pad <= 65536.
   if (k_pad <= 512)

@@ -287,14 +287,16 @@ int ozk_gemm_stats(unsigned long long* out8);
 int ozk_selftest_timeout(int budget_ms, int32_t* status_dev, int32_t* ok_dev, void* stream);
 /* L2 residency of the slice GEMM's running sums (no counterpart in the
  * reference).  The 256-wide GEMM tiles keep per-CTA running sums in a global
- * scratch (ozk_slice_gemm_workspace_bytes, about 37 MB) that it re-reads every
+ * scratch (ozk_slice_gemm_workspace_bytes, about 38 MB) that it re-reads every
  * pair, and it marks those accesses evict_last.  That priority takes effect
- * only inside the context's persisting-L2 set-aside, which is 0 by default.
- * This sets the set-aside of the current device's context to `bytes` (clamped
- * to the device maximum; 0 turns it off) and returns the value in force
- * before in *previous (may be NULL).  The limit belongs to this process's CUDA
- * context and ends with it; it reduces the L2 left to other kernels of the
- * process by the same amount. */
+ * only inside the context's persisting-L2 set-aside.  The library raises the
+ * set-aside to hold the sums on its first 256-wide GEMM launch on a device
+ * (never lowering it; OZK_L2_PERSIST=0 in the environment leaves it alone,
+ * OZK_L2_PERSIST=<MB> asks for that size).  This call sets it explicitly:
+ * `bytes` (clamped to the device maximum; 0 turns it off; (size_t)-1 only
+ * queries), the value in force before goes to *previous (may be NULL).  The
+ * limit belongs to this process's CUDA context and ends with it; lines not
+ * marked persisting may use the set-aside while no persisting data holds it. */
 int ozk_set_l2_persisting(size_t bytes, size_t* previous);
 /* Library version string. */
 const char* ozk_version(void);

@@ -716,10 +716,11 @@ int ozk_set_l2_persisting(size_t bytes, size_t* previous) {
   int mx = 0;
   if ((e = cudaDeviceGetAttribute(&mx, cudaDevAttrMaxPersistingL2CacheSize, dev)) != cudaSuccess)
     return set_cuda_error("cudaDeviceGetAttribute(max persisting L2)", e);
+  if (previous) *previous = prev;
+  if (bytes == (size_t)-1) return OZK_OK;  // query only
   if (bytes > (size_t)mx) bytes = (size_t)mx;
   if ((e = cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, bytes)) != cudaSuccess)
     return set_cuda_error("cudaDeviceSetLimit(persisting L2)", e);
-  if (previous) *previous = prev;
   return OZK_OK;
 }
 

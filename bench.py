@@ -42,6 +42,14 @@ METRIC = "FP64-equiv TFLOP/s (2MNK/t) at 8192^3 high + normwise rel err"
 PRESETS = {"high": (4, 1), "medium": (3, 1), "max": (5, 4)}
 
 
+# DRAM bytes (read + write) of one slice-GEMM launch of the default workload,
+# from one capture of this command on a B200:
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none \
+#       -k regex:k_slice_gemm -c 1 python bench.py --steps 2 --warmup 1
+# (11.16 GB read + 0.51 GB written).  Other workloads report null.
+GEMM_TRAFFIC_BYTES = {(8192, "high", "int8"): 11.67e9}
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -364,7 +372,9 @@ def ours(args):
                          "achieved": gemm_tflops, "peak": mma_peak,
                          "unit": "TOP/s" if s8 else "TFLOP/s",
                          "frac": gemm_tflops / mma_peak, "peak_source": peak_src,
-                         "traffic": None,
+                         "traffic": GEMM_TRAFFIC_BYTES.get(
+                             (n, args.precision, "int8" if s8 else "bf16")) if world == 1 else None,
+                         "traffic_unit": "bytes per launch (ncu dram__bytes_read+write)",
                          "extract": {"bound": "hbm", "achieved_gbs": ext_bytes / (extract_ms * 1e-3) / 1e9,
                                      "peak_gbs": hbm_peak,
                                      "frac": ext_bytes / (extract_ms * 1e-3) / 1e9 / hbm_peak}},

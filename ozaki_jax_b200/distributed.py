@@ -8,8 +8,9 @@ the single-GPU result.  B reaches every rank in one of two ways:
 
   b_source='replicated'  every rank was given B and extracts its column slices
                          locally (no collective in the data path);
-  b_source='root'        rank 0 extracts B's slices once and broadcasts the BF16
-                         slice stack and exponents over NCCL (NVLink).
+  b_source='root'        rank 0 extracts B's slices once and broadcasts the slice
+                         stack (int8 codes where exact, else BF16) and exponents
+                         over NCCL (NVLink).
 
 The collectives go through torch.distributed (NCCL for CUDA tensors, gloo on
 CPU); the compute is libozaki_b200.
@@ -93,33 +94,73 @@ def matmul_rowsharded(A_local, B, K=None, precision="high", b_source="replicated
     if Kb != Kd:
         raise ValueError(f"Incompatible shapes for matmul: {tuple(Ad.shape)} and {(Kb, M)}.")
     rho = compute_rho_f32(Kd)
-    k_pad = (max(Kd, 1) + 63) // 64 * 64
     sh = D.stream_handle(dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    SB = torch.empty((nS, M, k_pad), dtype=torch.int16, device=dev)
-    eB = torch.empty((nS, M), dtype=torch.int32, device=dev)
-    if b_source == "replicated" or rank == 0:
-        Bd = B.to(device=dev, dtype=torch.float64).contiguous()
-        BT = torch.empty((M, Kd), dtype=torch.float64, device=dev)
-        L.check(lib.ozk_extract_cols_f64(Bd.data_ptr(), Bd.stride(0), Kd, M, rho, n_hi, n_lo,
-                                         SB.data_ptr(), k_pad, eB.data_ptr(), BT.data_ptr(),
-                                         BT.numel() * 8, status.data_ptr(), sh))
-    if b_source == "root":
-        dist.broadcast(SB, src=0, group=group)
-        dist.broadcast(eB, src=0, group=group)
-    SA = torch.empty((nS, nb, k_pad), dtype=torch.int16, device=dev)
-    eA = torch.empty((nS, nb), dtype=torch.int32, device=dev)
     C = torch.empty((nb, M), dtype=torch.float64, device=dev)
-    if nb > 0:
-        L.check(lib.ozk_extract_rows_f64(Ad.data_ptr(), Ad.stride(0), nb, Kd, rho, n_hi, n_lo,
-                                         SA.data_ptr(), k_pad, eA.data_ptr(), status.data_ptr(),
-                                         sh))
-        pa, pb, npairs = _pairs(lib, n_hi, n_lo)
-        GW = torch.empty(lib.ozk_slice_gemm_workspace_bytes(), dtype=torch.uint8, device=dev)
-        L.check(lib.ozk_slice_gemm(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(), eB.data_ptr(),
-                                   nS, nb, M, k_pad, pa, pb, npairs, L.OZK_ACC_FIXED, 0, 1.0, 0.0,
-                                   None, 0, C.data_ptr(), M, None, GW.data_ptr(), GW.numel(), rho,
-                                   status.data_ptr(), sh))
+    pa, pb, npairs = _pairs(lib, n_hi, n_lo)
+    GW = torch.empty(lib.ozk_slice_gemm_workspace_bytes(), dtype=torch.uint8, device=dev)
+    have_b = b_source == "replicated" or rank == 0
+    Bd = B.to(device=dev, dtype=torch.float64).contiguous() if have_b else None
+    BT = torch.empty((M, Kd), dtype=torch.float64, device=dev) if have_b else None
+
+    # int8 slice codes (exact for rho >= 19) when every rank's GEMM can take them;
+    # the ranks agree on the format of B's slices before any is broadcast.
+    use_s8 = rho >= 19 and M >= 256
+    if use_s8:
+        nbmin = torch.tensor([nb], dtype=torch.int64, device=dev)
+        dist.all_reduce(nbmin, op=dist.ReduceOp.MIN, group=group)
+        use_s8 = int(nbmin.item()) >= 256
+    if use_s8:
+        k8 = (Kd + 127) // 128 * 128
+        fail = torch.zeros(1, dtype=torch.int32, device=dev)
+        SB = torch.empty((nS, M, k8), dtype=torch.int8, device=dev)
+        eB = torch.empty((nS, M), dtype=torch.int32, device=dev)
+        if have_b:
+            L.check(lib.ozk_extract_cols_s8_f64(Bd.data_ptr(), Bd.stride(0), Kd, M, rho, n_hi,
+                                                n_lo, SB.data_ptr(), k8, eB.data_ptr(),
+                                                BT.data_ptr(), BT.numel() * 8, fail.data_ptr(),
+                                                status.data_ptr(), sh))
+        if b_source == "root":
+            dist.broadcast(SB, src=0, group=group)
+            dist.broadcast(eB, src=0, group=group)
+            dist.broadcast(fail, src=0, group=group)
+        SA = torch.empty((nS, nb, k8), dtype=torch.int8, device=dev)
+        eA = torch.empty((nS, nb), dtype=torch.int32, device=dev)
+        L.check(lib.ozk_extract_rows_s8_f64(Ad.data_ptr(), Ad.stride(0), nb, Kd, rho, n_hi, n_lo,
+                                            SA.data_ptr(), k8, eA.data_ptr(), fail.data_ptr(),
+                                            status.data_ptr(), sh))
+        # a code without an exact int8 value anywhere sends every rank to BF16
+        dist.all_reduce(fail, op=dist.ReduceOp.MAX, group=group)
+        if int(fail.item()) == 0:
+            L.check(lib.ozk_slice_gemm_s8(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(),
+                                          eB.data_ptr(), nS, nb, M, k8, pa, pb, npairs, 0, 1.0,
+                                          0.0, None, 0, C.data_ptr(), M, GW.data_ptr(), GW.numel(),
+                                          rho, None, status.data_ptr(), sh))
+        else:
+            use_s8 = False
+        del SA, SB
+    if not use_s8:
+        k_pad = (max(Kd, 1) + 63) // 64 * 64
+        SB = torch.empty((nS, M, k_pad), dtype=torch.int16, device=dev)
+        eB = torch.empty((nS, M), dtype=torch.int32, device=dev)
+        if have_b:
+            L.check(lib.ozk_extract_cols_f64(Bd.data_ptr(), Bd.stride(0), Kd, M, rho, n_hi, n_lo,
+                                             SB.data_ptr(), k_pad, eB.data_ptr(), BT.data_ptr(),
+                                             BT.numel() * 8, status.data_ptr(), sh))
+        if b_source == "root":
+            # NCCL has no 16-bit integer type: move the BF16 bit patterns as bytes
+            dist.broadcast(SB.view(torch.uint8), src=0, group=group)
+            dist.broadcast(eB, src=0, group=group)
+        SA = torch.empty((nS, nb, k_pad), dtype=torch.int16, device=dev)
+        eA = torch.empty((nS, nb), dtype=torch.int32, device=dev)
+        if nb > 0:
+            L.check(lib.ozk_extract_rows_f64(Ad.data_ptr(), Ad.stride(0), nb, Kd, rho, n_hi, n_lo,
+                                             SA.data_ptr(), k_pad, eA.data_ptr(), status.data_ptr(),
+                                             sh))
+            L.check(lib.ozk_slice_gemm(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(),
+                                       eB.data_ptr(), nS, nb, M, k_pad, pa, pb, npairs,
+                                       L.OZK_ACC_FIXED, 0, 1.0, 0.0, None, 0, C.data_ptr(), M,
+                                       None, GW.data_ptr(), GW.numel(), rho, status.data_ptr(), sh))
     flags = int(status.item())
     if flags:
         raise ValueError("Ozaki preflight marked this input as unsafe: inputs contain NaN or Inf"

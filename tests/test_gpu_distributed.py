@@ -3,7 +3,9 @@ rank's rows of C equal the single-GPU result bit for bit, for B replicated
 and for B's slices broadcast from the root."""
 
 import os
+import queue
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -35,16 +37,18 @@ def _worker(rank, world, port, q):
         import ozaki_jax_b200 as oz
         from ozaki_jax_b200.distributed import gather_rows, matmul_rowsharded, row_range
         rng = np.random.RandomState(0)
-        A, B = rng.randn(600, 700), rng.randn(700, 500)
-        ref = oz.matmul(A, B, pipeline="ondevice")  # single-GPU result on this device
-        r0, r1 = row_range(600, rank, world)
-        Ad = torch.as_tensor(A[r0:r1]).to(dev)
         out = {}
-        for src in ("replicated", "root"):
-            Bd = torch.as_tensor(B).to(dev) if (src == "replicated" or rank == 0) else None
-            C = matmul_rowsharded(Ad, Bd, b_source=src)
-            full = gather_rows(C, 600)
-            out[src] = bool(np.array_equal(full.cpu().numpy(), ref))
+        # K = 700: BF16 slices; K = 5000 (rho 19, 600 rows per rank): int8 codes
+        for n, k, m in ((600, 700, 500), (1200, 5000, 600)):
+            A, B = rng.randn(n, k), rng.randn(k, m)
+            ref = oz.matmul(A, B, pipeline="ondevice")  # single-GPU result on this device
+            r0, r1 = row_range(n, rank, world)
+            Ad = torch.as_tensor(A[r0:r1]).to(dev)
+            for src in ("replicated", "root"):
+                Bd = torch.as_tensor(B).to(dev) if (src == "replicated" or rank == 0) else None
+                C = matmul_rowsharded(Ad, Bd, b_source=src)
+                full = gather_rows(C, n)
+                out[(k, src)] = bool(np.array_equal(full.cpu().numpy(), ref))
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
@@ -58,9 +62,17 @@ def test_rowsharded_matmul_two_gpus():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=300) for _ in procs]
+    res = []
+    deadline = time.monotonic() + 300
+    while len(res) < len(procs):
+        try:
+            res.append(q.get(timeout=5))
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            assert not dead, f"a rank exited with {dead}"
+            assert time.monotonic() < deadline, "ranks did not finish"
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     for _, out in res:
-        assert out == {"replicated": True, "root": True}
+        assert len(out) == 4 and all(out.values()), out

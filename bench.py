@@ -393,6 +393,114 @@ def ours(args):
         dist.destroy_process_group()
 
 
+WORKLOADS = {
+    # name: (description, precision)
+    "c3": ("matmul 4096x8192x4096 precision=max, (U(0,1)-0.5)*exp(10*N(0,1)) entries", "max"),
+    "c4": ("gram A^T A, A 65536x4096 N(0,1), column j scaled by 10^(-6j/4095)", "high"),
+    "c5a": ("matmul 32768^3 precision=medium, N(0,1)", "medium"),
+    "c5b": ("residual b - A x, A 32768^2 N(0,1) + 32768 I, x, b 32768x16", "high"),
+}
+
+
+def other_workload(args):
+    """The other BASELINE configurations on one GPU, through the C entry points
+    on device arrays (inputs drawn on the device from a seeded torch generator
+    with the distributions BASELINE describes).  Prints one JSON line."""
+    import torch
+    from ozaki_jax_b200 import _lib
+
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    desc, precision = WORKLOADS[args.workload]
+    n_hi, n_lo = PRESETS[precision]
+    n_pairs = n_hi * n_hi + 2 * n_hi * n_lo
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    randn = lambda *shape: torch.randn(*shape, generator=g, device=dev, dtype=torch.float64)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    sh = torch.cuda.current_stream(dev).cuda_stream
+    w = args.workload
+    if w in ("c3", "c5a"):
+        n, k, m = (4096, 8192, 4096) if w == "c3" else (32768, 32768, 32768)
+        if w == "c3":
+            A = (torch.rand(n, k, generator=g, device=dev, dtype=torch.float64) - 0.5) * torch.exp(10 * randn(n, k))
+            B = (torch.rand(k, m, generator=g, device=dev, dtype=torch.float64) - 0.5) * torch.exp(10 * randn(k, m))
+        else:
+            A, B = randn(n, k), randn(k, m)
+        C = torch.empty((n, m), dtype=torch.float64, device=dev)
+        ws = torch.empty(lib.ozk_matmul_workspace_bytes(n, k, m, n_hi, n_lo), dtype=torch.uint8, device=dev)
+        call = lambda: _lib.check(lib.ozk_matmul_f64(
+            A.data_ptr(), k, B.data_ptr(), m, C.data_ptr(), m, n, k, m, -1, n_hi, n_lo,
+            _lib.OZK_ACC_FIXED, ws.data_ptr(), ws.numel(), st.data_ptr(), sh))
+        flops, contraction, ref = 2.0 * n * k * m, k, (lambda: torch.matmul(A, B))
+    elif w == "c4":
+        n, k = 65536, 4096
+        A = randn(n, k) * torch.pow(10.0, -6.0 * torch.arange(k, device=dev, dtype=torch.float64) / 4095)
+        C = torch.empty((k, k), dtype=torch.float64, device=dev)
+        ws = torch.empty(lib.ozk_gram_workspace_bytes(n, k, n_hi, n_lo), dtype=torch.uint8, device=dev)
+        call = lambda: _lib.check(lib.ozk_gram_f64(
+            A.data_ptr(), k, C.data_ptr(), k, n, k, -1, n_hi, n_lo, ws.data_ptr(), ws.numel(),
+            st.data_ptr(), sh))
+        flops, contraction, ref = 2.0 * n * k * k, n, (lambda: torch.matmul(A.T, A))
+    else:
+        n, m = 32768, 16
+        k = n
+        A = randn(n, n)
+        A.diagonal().add_(float(n))
+        X, Bv = randn(n, m), randn(n, m)
+        C = torch.empty((n, m), dtype=torch.float64, device=dev)
+        ws = torch.empty(lib.ozk_residual_workspace_bytes(n, n, m, n_hi, n_lo), dtype=torch.uint8, device=dev)
+        call = lambda: _lib.check(lib.ozk_residual_f64(
+            A.data_ptr(), n, X.data_ptr(), m, Bv.data_ptr(), m, C.data_ptr(), m, n, n, m, -1,
+            n_hi, n_lo, ws.data_ptr(), ws.numel(), st.data_ptr(), sh))
+        flops, contraction, ref = 2.0 * n * n * m, n, (lambda: Bv - torch.matmul(A, X))
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize(dev)
+    assert st.item() == 0, f"device status {st.item()}"
+    clocks = Clocks(0)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    R = ref()
+    rel_err = float(torch.linalg.norm(C - R) / torch.linalg.norm(R))
+    del R
+    rho = lib.ozk_compute_rho_f32(contraction)
+    s8 = rho >= 19
+    bf16_peak, hbm_peak, src = peaks()
+    out = {"metric": "FP64-equiv TFLOP/s (2MNK/t)" if w != "c4" else "FP64-equiv TFLOP/s (2NK^2/t)",
+           "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+           "higher_is_better": True, "dtype": "f64", "data": "synthetic (torch CUDA generator, seed 0)",
+           "config": {"workload": f"{w}: {desc}", "precision": precision,
+                      "slices": "int8 codes" if s8 else "bf16", "rho": rho},
+           "rel_err_vs_cublas_dgemm": rel_err, "clocks": clk}
+    if w == "c5b":
+        a_bytes = 8.0 * n * n
+        out["roofline"] = {"bound": "hbm", "achieved": a_bytes / (ms * 1e-3) / 1e9,
+                           "peak": hbm_peak, "unit": "GB/s", "frac": a_bytes / (ms * 1e-3) / 1e9 / hbm_peak,
+                           "note": "algorithmic bytes = one read of A", "peak_source": src}
+    else:
+        tensor = n_pairs * flops
+        if w == "c4":
+            # only the tiles on or above the diagonal are computed
+            tiles = (k // 256) * (k // 256 + 1) / 2 / (k // 256) ** 2
+            tensor *= tiles
+        peak = 2 * bf16_peak if s8 else bf16_peak
+        out["roofline"] = {"bound": "tensor", "achieved": tensor / (ms * 1e-3) / 1e12, "peak": peak,
+                           "unit": "TOP/s" if s8 else "TFLOP/s",
+                           "frac": tensor / (ms * 1e-3) / 1e12 / peak,
+                           "peak_source": ("2x " if s8 else "") + f"{src} sustained bf16"}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -406,8 +514,13 @@ def main():
     ap.add_argument("--l2-persist-mb", type=int, default=0,
                     help="persisting-L2 set-aside for the GEMM's running sums in MB "
                          "(0: the library's own choice)")
+    ap.add_argument("--workload", choices=["c2"] + sorted(WORKLOADS), default="c2",
+                    help="c2 (default): the headline 8192^3 line; others: the remaining "
+                         "BASELINE configurations on one GPU")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.workload != "c2" and args.impl == "ours":
+        other_workload(args)
+    elif args.impl == "reference":
         reference_arm(args)
     else:
         ours(args)

@@ -234,6 +234,42 @@ bool s8_enabled() {
 // extraction and GEMM are enqueued behind them gated on w.gate, so they run
 // (and overwrite the result) only if some slice had no exact int8 code.  The
 // stream never waits on the host for that decision.
+// C = alpha (A B) + beta Cin for at most 16 columns of B, with int8 codes and
+// the skinny all-pairs GEMM (each A slice read once), and the gated BF16
+// recomputation behind it.  Returns 1 when the request does not qualify.
+static int skinny_fixed(const double* A, int64_t lda, const double* B, int64_t ldb, double alpha,
+                        double beta, const double* Cin, int64_t ldcin, double* C, int64_t ldc,
+                        int64_t N, int64_t K, int64_t M, int rho, int n_hi, int n_lo,
+                        const uint8_t* pa, const uint8_t* pb, int np, const Workspace& w,
+                        int32_t* status_dev, cudaStream_t s) {
+  const int nS = n_hi + n_lo;
+  const int64_t k_pad = round_up(K, OZK_KB);
+  const int64_t k8 = round_up(K, kS8KB);
+  if (!skinny_s8_eligible(N, M, k8, nS, np, rho)) return 1;
+  int rc;
+  cudaError_t e = cudaMemsetAsync(w.gate, 0, sizeof(int32_t), s);
+  if (e != cudaSuccess) return set_cuda_error("cudaMemsetAsync(gate)", e);
+  if ((rc = launch_extract_rows_s8(A, lda, N, K, rho, n_hi, n_lo, (int8_t*)w.SA, k8, w.eA,
+                                   status_dev, w.gate, s)))
+    return rc;
+  if ((rc = launch_extract_cols_s8(B, ldb, K, M, rho, n_hi, n_lo, (int8_t*)w.SB, k8, w.eB,
+                                   status_dev, w.gate, w.BT, s)))
+    return rc;
+  if ((rc = launch_skinny_s8((const int8_t*)w.SA, w.eA, (const int8_t*)w.SB, w.eB, nS, N, M, k8,
+                             pa, pb, np, alpha, beta, Cin, ldcin, C, ldc, rho, status_dev, w.gate,
+                             0, s)))
+    return rc;
+  if ((rc = launch_extract_rows_gated(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev,
+                                      w.gate, s)))
+    return rc;
+  if ((rc = launch_extract_rows_gated(w.BT, K, M, K, rho, n_hi, n_lo, w.SB, k_pad, w.eB,
+                                      status_dev, w.gate, s)))
+    return rc;
+  return launch_slice_gemm_ex(w.SA, w.eA, nS, w.SB, w.eB, nS, N, M, k_pad, pa, pb, np,
+                              OZK_ACC_FIXED, 0, alpha, beta, Cin, ldcin, C, ldc, nullptr, w.state,
+                              w.state_bytes, rho, status_dev, false, w.gate, 1, s);
+}
+
 static int matmul_fixed(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
                         int64_t ldc, int64_t N, int64_t K, int64_t M, int rho, int n_hi, int n_lo,
                         const uint8_t* pa, const uint8_t* pb, int np, const Workspace& w,
@@ -242,6 +278,11 @@ static int matmul_fixed(const double* A, int64_t lda, const double* B, int64_t l
   const int64_t k_pad = round_up(K, OZK_KB);
   const int64_t k8 = round_up(K, kS8KB);
   int rc;
+  if (s8_enabled() && M <= 16) {
+    rc = skinny_fixed(A, lda, B, ldb, 1.0, 0.0, nullptr, 0, C, ldc, N, K, M, rho, n_hi, n_lo, pa,
+                      pb, np, w, status_dev, s);
+    if (rc != 1) return rc;
+  }
   if (!s8_enabled() || !slice_gemm_s8_eligible(N, M, k8, OZK_ACC_FIXED, rho, w.state_bytes)) {
     if ((rc = launch_extract_rows(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
       return rc;
@@ -662,6 +703,11 @@ int ozk_residual_f64(const double* A, int64_t lda, const double* X, int64_t ldx,
   ScopedWs ws;
   if ((rc = ws.acquire(workspace, workspace ? ws_bytes : need, need, s))) return rc;
   Workspace w = layout(ws.ptr, N, K, M, nS, 0, M * K, sb);
+  if (s8_enabled() && M <= 16) {
+    rc = skinny_fixed(A, lda, X, ldx, -1.0, 1.0, Bv, ldb, R, ldr, N, K, M, rho, n_hi, n_lo, pa, pb,
+                      np, w, status_dev, s);
+    if (rc != 1) return rc;
+  }
   if ((rc = launch_extract_rows(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev, s)))
     return rc;
   if ((rc = launch_extract_cols(X, ldx, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, status_dev, w.BT,

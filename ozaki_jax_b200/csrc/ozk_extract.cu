@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
 // FP32 range) set *s8_fail instead, once per line.
 constexpr uint32_t kBulkChunk = 16384;  // bytes per bulk copy instruction
 
-template <int NT, int EPT, int MINB, bool S8>
+template <int NT, int EPT, int MINB, bool S8, int CL>
 __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
     const double* __restrict__ X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
     int n_lo, void* __restrict__ slices_v, int64_t k_pad, int32_t* __restrict__ exps,
@@ -348,9 +348,15 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ uint64_t s_bar;
   __shared__ float s_part[2][2][NW];  // [parity][hi, lo][warp]
+  __shared__ float s_cta[2][3];       // [parity][hi max, lo max, line flags] for the cluster
   __shared__ int s_abort;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t row_bytes = (uint32_t)(K * 8);
+  const uint32_t crank = CL > 1 ? cluster_ctarank() : 0;
+  // This CTA's columns of every row: [kbase, kbase + NT*EPT) of [0, K).
+  const int64_t kbase = (int64_t)crank * NT * EPT;
+  const int64_t kown = K - kbase < (int64_t)NT * EPT ? (K - kbase > 0 ? K - kbase : 0)
+                                                      : (int64_t)NT * EPT;
+  const uint32_t own_bytes = (uint32_t)(kown * 8);
   const int npass = n_hi > n_lo ? n_hi : n_lo;
   const int64_t slice_stride = rows * k_pad;
   const double* xb = reinterpret_cast<const double*>(smem_raw);
@@ -362,37 +368,44 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
   }
   __syncthreads();
   auto issue = [&](int64_t row) {
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(X + row * ldx);
-    mbar_arrive_expect_tx(&s_bar, row_bytes);
-    for (uint32_t off = 0; off < row_bytes; off += kBulkChunk)
-      bulk_load_g2s(smem_raw + off, src + off, min(kBulkChunk, row_bytes - off), &s_bar);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(X + row * ldx + kbase);
+    mbar_arrive_expect_tx(&s_bar, own_bytes);
+    for (uint32_t off = 0; off < own_bytes; off += kBulkChunk)
+      bulk_load_g2s(smem_raw + off, src + off, min(kBulkChunk, own_bytes - off), &s_bar);
   };
+  // A cluster's CTAs go through every row together.  If a wait runs out of
+  // time the CTA keeps stepping with its peers (so no cluster barrier is left
+  // waiting) but issues no more copies; the timeout flag reports the failure.
+  const int64_t row0 = blockIdx.x / CL, rstride = gridDim.x / CL;
   uint32_t issued = 0;  // rows whose copy was issued (thread 0's count)
-  if (tid == 0 && (int64_t)blockIdx.x < rows) {
-    issue(blockIdx.x);
+  uint32_t landed = 0;  // rows whose copy was waited for
+  bool live = true;     // no wait has run out of time (uniform over the CTA)
+  if (tid == 0 && row0 < rows && own_bytes) {
+    issue(row0);
     ++issued;
   }
   uint32_t it = 0, par = 0;
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
-    // All threads wait for the row; the decision to go on is taken together,
-    // so no thread can reach a barrier the others have left.
-    const bool got = mbar_wait(&s_bar, it & 1, (volatile int*)&s_abort, status, budget_ns);
-    if (__syncthreads_or(!got)) break;
+  for (int64_t row = row0; row < rows; row += rstride, ++it) {
+    bool got = true;
+    if (live && own_bytes)
+      got = mbar_wait(&s_bar, it & 1, (volatile int*)&s_abort, status, budget_ns);
+    if (__syncthreads_or(!got)) live = false;
+    else if (live && own_bytes) ++landed;
     float rh[EPT], rl[EPT];
     float mh = 0.0f, ml = 0.0f;
     int32_t flags = 0;
 #pragma unroll
     for (int q = 0; q < NG; ++q) {
-      const int64_t k = 4 * ((int64_t)q * NT + tid);
+      const int64_t k = 4 * ((int64_t)q * NT + tid);  // within this CTA's columns
       double x[4] = {0.0, 0.0, 0.0, 0.0};
-      if (k + 3 < K) {
+      if (k + 3 < kown) {
         const double2 a2 = *reinterpret_cast<const double2*>(xb + k);
         const double2 b2 = *reinterpret_cast<const double2*>(xb + k + 2);
         x[0] = a2.x, x[1] = a2.y, x[2] = b2.x, x[3] = b2.y;
       } else {
 #pragma unroll
         for (int h = 0; h < 4; ++h)
-          if (k + h < K) x[h] = xb[k + h];
+          if (k + h < kown) x[h] = xb[k + h];
       }
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
@@ -405,17 +418,18 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
       }
     }
     if (flags) raise_flag(status, flags);
-    // The buffer is free: fetch this CTA's next row while slicing this one.
-    const int line_bad = __syncthreads_or(flags);
-    if (tid == 0) {
-      const int64_t nx = row + (int64_t)gridDim.x;
+    // The buffer is free: fetch this CTA's share of its next row while slicing
+    // this one.
+    int line_bad = __syncthreads_or(flags);
+    if (tid == 0 && live && own_bytes) {
+      const int64_t nx = row + rstride;
       if (nx < rows) {
         fence_proxy_async_smem();
         issue(nx);
         ++issued;
       }
     }
-    bool bad = S8 && line_bad;
+    bool bad = false;
     for (int t = 0; t < npass; ++t, par ^= 1) {
       const bool do_hi = t < n_hi, do_lo = t < n_lo;
 #pragma unroll
@@ -433,6 +447,22 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         mh = fmaxf(mh, s_part[par][0][w]);
         ml = fmaxf(ml, s_part[par][1][w]);
       }
+      if constexpr (CL > 1) {
+        // line maxima (and, in the first pass, the line's input flags) over
+        // the cluster through distributed shared memory
+        if (tid == 0) {
+          s_cta[par][0] = mh;
+          s_cta[par][1] = ml;
+          s_cta[par][2] = (float)line_bad;
+        }
+        cluster_sync();
+        for (uint32_t r = 0; r < (uint32_t)CL; ++r) {
+          mh = fmaxf(mh, ld_dsmem_f32(&s_cta[par][0], r));
+          ml = fmaxf(ml, ld_dsmem_f32(&s_cta[par][1], r));
+          if (t == 0 && ld_dsmem_f32(&s_cta[par][2], r) != 0.0f) line_bad = 1;
+        }
+      }
+      if (t == 0) bad = S8 && line_bad;
       float sh = 0.f, ih = 0.f, sl = 0.f, il = 0.f;
       int zh = 1, zl = 1, ch = 0, cl = 0;
       if (do_hi) slice_params(mh, rho, sh, ih, zh, ch);
@@ -441,7 +471,7 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         if (do_hi && !zh && (ch < -127 || rho + ch > 127)) bad = true;
         if (do_lo && !zl && (cl < -127 || rho + cl > 127)) bad = true;
       }
-      if (tid == 0) {
+      if (tid == 0 && crank == 0) {
         if (do_hi) exps[(int64_t)t * rows + row] = ch;
         if (do_lo) exps[(int64_t)(n_hi + t) * rows + row] = cl;
       }
@@ -451,7 +481,7 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
       const int64_t off_l = (int64_t)(n_hi + t) * slice_stride + row * k_pad;
 #pragma unroll
       for (int q = 0; q < NG; ++q) {
-        const int64_t k = 4 * ((int64_t)q * NT + tid);
+        const int64_t k = kbase + 4 * ((int64_t)q * NT + tid);  // column in the row
 #pragma unroll
         for (int side = 0; side < 2; ++side) {
           if (side == 0 ? !do_hi : !do_lo) continue;
@@ -489,14 +519,15 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         }
       }
     }
-    if (S8 && bad && tid == 0) *s8_fail = 1;
+    if (S8 && bad && tid == 0 && crank == 0) *s8_fail = 1;
   }
   // Every issued copy lands before the CTA's shared memory is released.
   if (tid == 0) {
-    for (uint32_t j = it; j < issued; ++j)
+    for (uint32_t j = landed; j < issued; ++j)
       mbar_wait(&s_bar, j & 1, nullptr, status, budget_ns);
   }
   __syncthreads();
+  if constexpr (CL > 1) cluster_sync();  // peers may still read this CTA's s_cta
 }
 
 // ---------------------------------------------------------------- transpose
@@ -865,30 +896,44 @@ static int launch_rows_reg(const double* X, int64_t ldx, int64_t rows, int64_t K
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows_reg launch", e);
 }
 
-template <int NT, int EPT, int MINB, bool S8>
+template <int NT, int EPT, int MINB, bool S8, int CL = 1>
 static int launch_rows_bulk(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
                             int n_hi, int n_lo, void* slices, int64_t k_pad, int32_t* exps,
                             int32_t* status, int32_t* s8_fail, const int32_t* gate, int dev,
                             cudaStream_t stream) {
   constexpr size_t kMaxSmem = (size_t)EPT * NT * 8;
+  auto kern = k_extract_rows_bulk<NT, EPT, MINB, S8, CL>;
   static int configured[64] = {0};
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(k_extract_rows_bulk<NT, EPT, MINB, S8>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kMaxSmem);
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k_extract_rows_bulk)", e);
+    if (CL > 1) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     configured[dev] = 1;
   }
-  const size_t smem = (size_t)round_up(K * 8, 128);
+  // CTA r of a cluster stages columns [r*NT*EPT, (r+1)*NT*EPT) of a row
+  const size_t smem = (size_t)round_up((K < (int64_t)NT * EPT ? K : (int64_t)NT * EPT) * 8, 128);
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_extract_rows_bulk<NT, EPT, MINB, S8>,
-                                                    NT, smem) != cudaSuccess || per_sm < 1)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem) != cudaSuccess ||
+      per_sm < 1)
     per_sm = 1;
-  int64_t grid = (int64_t)device_sm_count(dev) * per_sm;
-  if (grid > rows) grid = rows;
-  k_extract_rows_bulk<NT, EPT, MINB, S8><<<(unsigned)grid, NT, smem, stream>>>(
-      X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps, status, s8_fail, gate,
-      wait_budget_ns());
-  cudaError_t e = cudaGetLastError();
+  int64_t clusters = (int64_t)device_sm_count(dev) * per_sm / CL;
+  if (clusters > rows) clusters = rows;
+  if (clusters < 1) clusters = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(clusters * CL));
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
+                                     exps, status, s8_fail, gate, wait_budget_ns());
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows_bulk launch", e);
 }
 
@@ -900,7 +945,7 @@ static bool bulk_rows_ok(const double* X, int64_t ldx, int64_t K, int64_t k_pad)
     const char* e = getenv("OZK_EXTRACT_BULK");
     on = (e && e[0] == '0') ? 0 : 1;
   }
-  return on && K > 1024 && k_pad <= 12288 && K % 2 == 0 && ldx % 2 == 0 &&
+  return on && K > 1024 && k_pad <= 65536 && K % 2 == 0 && ldx % 2 == 0 &&
          ((uintptr_t)X & 15) == 0;
 }
 
@@ -920,8 +965,16 @@ static int launch_rows_bulk_any(const double* X, int64_t ldx, int64_t rows, int6
   if (k_pad <= 8192)
     return launch_rows_bulk<256, 32, 2, S8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
                                             status, s8_fail, gate, dev, stream);
-  return launch_rows_bulk<512, 24, 1, S8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
-                                          status, s8_fail, gate, dev, stream);
+  if (k_pad <= 12288)
+    return launch_rows_bulk<512, 24, 1, S8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
+                                            status, s8_fail, gate, dev, stream);
+  // Longer rows: a cluster of CTAs per row, 16384 columns each, line maxima
+  // exchanged through distributed shared memory.
+  if (k_pad <= 32768)
+    return launch_rows_bulk<512, 32, 1, S8, 2>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
+                                               exps, status, s8_fail, gate, dev, stream);
+  return launch_rows_bulk<512, 32, 1, S8, 4>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
+                                             exps, status, s8_fail, gate, dev, stream);
 }
 
 int launch_extract_rows_s8(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,

@@ -1,6 +1,7 @@
 // Host-side internals shared by the library's translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -82,8 +83,21 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
 // 256-wide tiles with the state scratch, k_pad within the extraction limits).
 bool slice_gemm_s8_eligible(int64_t N, int64_t M, int64_t k_pad, int mode, int rho,
                             size_t state_bytes);
+// Skinny int8 slice GEMM (M <= 16 right-hand sides, fixed-point sums): every
+// pair product of a 128-row tile accumulates at once, so each A slice is read
+// once.  SX [nS][M][k8] int8 codes of X's columns, eX [nS][M].
+bool skinny_s8_eligible(int64_t N, int64_t M, int64_t k8, int nS, int n_pairs, int rho);
+int launch_skinny_s8(const int8_t* SA, const int32_t* eA, const int8_t* SX, const int32_t* eX,
+                     int nS, int64_t N, int64_t M, int64_t k8, const uint8_t* pair_a,
+                     const uint8_t* pair_b, int n_pairs, double alpha, double beta,
+                     const double* Cin, int64_t ldcin, double* C, int64_t ldc, int rho,
+                     int32_t* status, const int32_t* gate, int gate_want, cudaStream_t stream);
 // int8 slices enabled (OZK_S8=0 in the environment turns them off).
 bool s8_enabled();
+// Tensor map over a [depth][rows][k_pad] slice stack (BF16, or int8 codes
+// with s8), box of 128 bytes x box_rows, 128-byte swizzle.
+int make_slice_map(CUtensorMap* map, const void* base, int64_t k_pad, int64_t rows, int depth,
+                   int box_rows, bool s8);
 // Bytes of the per-CTA FP64 state scratch the 256-wide GEMM tiles need.
 size_t gemm_state_bytes(int dev);
 // Smallest workspace ozk_matmul_f64 (OZK_ACC_F64) accepts: without the state

@@ -47,7 +47,8 @@ def test_slices_match_reference_goldens(golden, name):
 @pytest.mark.parametrize("shape,seed,wide", [((300, 2000), 1, False), ((256, 8192), 2, False),
                                              ((97, 4100), 3, True), ((2, 70000), 4, False),
                                              ((300, 12000), 8, True), ((41, 3001), 9, False),
-                                             ((700, 1026), 10, True)])
+                                             ((700, 1026), 10, True), ((33, 16000), 11, True),
+                                             ((50, 20000), 12, False), ((40, 40000), 13, True)])
 def test_rows_match_oracle(shape, seed, wide):
     rng = np.random.RandomState(seed)
     X = rng.randn(*shape)

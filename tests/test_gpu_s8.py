@@ -218,3 +218,57 @@ def test_extreme_row_is_nan_like_the_reference(K, scale):
     assert np.array_equal(np.isnan(C), np.isnan(R))
     ok = ~np.isnan(R)
     assert O.rel_err(C[ok].reshape(-1, 30), R[ok].reshape(-1, 30)) <= 1e-12
+
+
+def bf16_residual(A, X, Bv, n_hi, n_lo):
+    """b - A X with fixed-point sums on BF16 slices (standalone entry points)."""
+    rho = O.compute_rho_f32(A.shape[1])
+    SA, k_pad, eA, _ = extract_device(torch.as_tensor(A).cuda(), rho, n_hi, n_lo, 1)
+    SX, _, eX, _ = extract_device(torch.as_tensor(X).cuda(), rho, n_hi, n_lo, 0)
+    return bf16_fixed_gemm(SA, eA, SX, eX, k_pad, A.shape[0], X.shape[1], rho, n_hi, n_lo,
+                           alpha=-1.0, beta=1.0, Cin=torch.as_tensor(Bv).cuda())
+
+
+def residual_pipeline(A, X, Bv, n_hi, n_lo):
+    lib = L.load()
+    N, K = A.shape
+    M = X.shape[1]
+    Ad, Xd, Bd = (torch.as_tensor(v).cuda() for v in (A, X, Bv))
+    R = torch.full((N, M), float("nan"), dtype=torch.float64, device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L.check(lib.ozk_residual_f64(Ad.data_ptr(), K, Xd.data_ptr(), M, Bd.data_ptr(), M,
+                                 R.data_ptr(), M, N, K, M, -1, n_hi, n_lo, None, 0, st.data_ptr(),
+                                 stream()))
+    torch.cuda.synchronize()
+    return R.cpu().numpy(), int(st.item())
+
+
+@pytest.mark.parametrize("N,K,M,n_hi,n_lo", [(1000, 5000, 16, 4, 1), (300, 4224, 5, 4, 1),
+                                             (777, 6000, 1, 3, 1), (256, 8192, 16, 4, 2)])
+def test_skinny_s8_residual_matches_bf16(N, K, M, n_hi, n_lo):
+    """Residuals (at most 16 right-hand sides) take the int8 all-pairs kernel;
+    bit-identical to the BF16 narrow kernel's fixed-point result."""
+    rng = np.random.RandomState(N + M)
+    A = rng.randn(N, K) * np.exp(rng.randn(N, 1) * 2)
+    X, Bv = rng.randn(K, M), rng.randn(N, M)
+    R, st = residual_pipeline(A, X, Bv, n_hi, n_lo)
+    assert st == 0
+    assert same(R, bf16_residual(A, X, Bv, n_hi, n_lo))
+
+
+@pytest.mark.parametrize("M", [16, 3])
+def test_skinny_s8_matmul_matches_bf16(M):
+    rng = np.random.RandomState(M)
+    A, B = rng.randn(2000, 4500), rng.randn(4500, M)
+    C, st = pipeline(A, B)
+    assert st == 0
+    assert same(C, bf16_pipeline(A, B, 4, 1))
+
+
+def test_skinny_s8_falls_back_on_device():
+    rng = np.random.RandomState(12)
+    A, X, Bv = rng.randn(300, 4200), rng.randn(4200, 8), rng.randn(300, 8)
+    A[5] *= 2.0 ** -135
+    R, _ = residual_pipeline(A, X, Bv, 4, 1)
+    assert same(R, bf16_residual(A, X, Bv, 4, 1))
+    assert np.isnan(R[5]).all() and not np.isnan(np.delete(R, 5, axis=0)).any()

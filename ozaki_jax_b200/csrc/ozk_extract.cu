@@ -342,13 +342,16 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
     int n_lo, void* __restrict__ slices_v, int64_t k_pad, int32_t* __restrict__ exps,
     int32_t* status, int32_t* s8_fail, const int32_t* gate, uint64_t budget_ns) {
   static_assert(EPT % 4 == 0, "EPT must be a multiple of 4");
+  static_assert(NT / 32 <= 32, "one warp reduces the warp partials");
   constexpr int NG = EPT / 4;
   constexpr int NW = NT / 32;
+  constexpr int ESZ = S8 ? 1 : 2;  // bytes per slice element
   if (gate && *(volatile const int32_t*)gate == 0) return;  // uniform over the grid
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ uint64_t s_bar;
-  __shared__ float s_part[2][2][NW];  // [parity][hi, lo][warp]
-  __shared__ float s_cta[2][3];       // [parity][hi max, lo max, line flags] for the cluster
+  __shared__ float s_part[2][2][NW];    // [parity][hi, lo][warp]
+  __shared__ float s_cta[2][3];         // [parity][hi max, lo max, line flags] for the cluster
+  __shared__ __align__(16) float s_prm[2][8];  // [parity][sig, inv, zero, c (hi); same (lo)]
   __shared__ int s_abort;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t crank = CL > 1 ? cluster_ctarank() : 0;
@@ -360,6 +363,13 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
   const int npass = n_hi > n_lo ? n_hi : n_lo;
   const int64_t slice_stride = rows * k_pad;
   const double* xb = reinterpret_cast<const double*>(smem_raw);
+  // groups of this thread that lie inside [0, k_pad): q < nq
+  int nq = 0;
+  {
+    const int64_t left = k_pad - kbase - 4 * (int64_t)tid;
+    if (left > 0) nq = (int)((left + 4 * NT - 1) / (4 * NT));
+    if (nq > NG) nq = NG;
+  }
 
   if (tid == 0) {
     mbar_init(&s_bar, 1);
@@ -393,7 +403,7 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
     else if (live && own_bytes) ++landed;
     float rh[EPT], rl[EPT];
     float mh = 0.0f, ml = 0.0f;
-    int32_t flags = 0;
+    bool odd = false;  // a non-finite split value: the input is non-finite or beyond FP32
 #pragma unroll
     for (int q = 0; q < NG; ++q) {
       const int64_t k = 4 * ((int64_t)q * NT + tid);  // within this CTA's columns
@@ -412,15 +422,25 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         float& hi = rh[4 * q + h];
         float& lo = rl[4 * q + h];
         split_f64(x[h], hi, lo);
-        flags |= check_value(x[h], hi);
+        odd |= !(fabsf(hi) <= 3.402823466e38f);
         mh = fmaxf(mh, fabsf(hi));
         ml = fmaxf(ml, fabsf(lo));
       }
     }
-    if (flags) raise_flag(status, flags);
+    int32_t flags = 0;
+    if (odd) {  // rare: tell non-finite input from FP32 overflow
+#pragma unroll
+      for (int q = 0; q < NG; ++q)
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const int64_t k = 4 * ((int64_t)q * NT + tid) + h;
+          if (k < kown) flags |= check_value(xb[k], rh[4 * q + h]);
+        }
+      raise_flag(status, flags);
+    }
     // The buffer is free: fetch this CTA's share of its next row while slicing
     // this one.
-    int line_bad = __syncthreads_or(flags);
+    const int line_bad = __syncthreads_or(flags);
     if (tid == 0 && live && own_bytes) {
       const int64_t nx = row + rstride;
       if (nx < rows) {
@@ -429,9 +449,10 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         ++issued;
       }
     }
-    bool bad = false;
     for (int t = 0; t < npass; ++t, par ^= 1) {
       const bool do_hi = t < n_hi, do_lo = t < n_lo;
+      // Line maxima: warp shuffles, then warp 0 over the warps (and the
+      // cluster), which also derives the slice parameters for everyone.
 #pragma unroll
       for (int o = 16; o; o >>= 1) {
         mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
@@ -442,11 +463,16 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         s_part[par][1][warp] = ml;
       }
       __syncthreads();
+      if (warp == 0) {
+        mh = lane < NW ? s_part[par][0][lane] : 0.0f;
+        ml = lane < NW ? s_part[par][1][lane] : 0.0f;
 #pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        mh = fmaxf(mh, s_part[par][0][w]);
-        ml = fmaxf(ml, s_part[par][1][w]);
+        for (int o = 16; o; o >>= 1) {
+          mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
+          ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, o));
+        }
       }
+      int lbad = line_bad;
       if constexpr (CL > 1) {
         // line maxima (and, in the first pass, the line's input flags) over
         // the cluster through distributed shared memory
@@ -456,70 +482,85 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
           s_cta[par][2] = (float)line_bad;
         }
         cluster_sync();
-        for (uint32_t r = 0; r < (uint32_t)CL; ++r) {
-          mh = fmaxf(mh, ld_dsmem_f32(&s_cta[par][0], r));
-          ml = fmaxf(ml, ld_dsmem_f32(&s_cta[par][1], r));
-          if (t == 0 && ld_dsmem_f32(&s_cta[par][2], r) != 0.0f) line_bad = 1;
+        if (warp == 0) {
+          for (uint32_t r = 0; r < (uint32_t)CL; ++r) {
+            mh = fmaxf(mh, ld_dsmem_f32(&s_cta[par][0], r));
+            ml = fmaxf(ml, ld_dsmem_f32(&s_cta[par][1], r));
+            if (t == 0 && ld_dsmem_f32(&s_cta[par][2], r) != 0.0f) lbad = 1;
+          }
         }
       }
-      if (t == 0) bad = S8 && line_bad;
-      float sh = 0.f, ih = 0.f, sl = 0.f, il = 0.f;
-      int zh = 1, zl = 1, ch = 0, cl = 0;
-      if (do_hi) slice_params(mh, rho, sh, ih, zh, ch);
-      if (do_lo) slice_params(ml, rho, sl, il, zl, cl);
-      if (S8) {
-        if (do_hi && !zh && (ch < -127 || rho + ch > 127)) bad = true;
-        if (do_lo && !zl && (cl < -127 || rho + cl > 127)) bad = true;
+      if (warp == 0 && lane == 0) {
+        float sh = 0.f, ih = 0.f, sl = 0.f, il = 0.f;
+        int zh = 1, zl = 1, ch = 0, cl = 0;
+        if (do_hi) slice_params(mh, rho, sh, ih, zh, ch);
+        if (do_lo) slice_params(ml, rho, sl, il, zl, cl);
+        if (S8) {
+          bool bad = t == 0 && lbad;
+          if (do_hi && !zh && (ch < -127 || rho + ch > 127)) bad = true;
+          if (do_lo && !zl && (cl < -127 || rho + cl > 127)) bad = true;
+          if (bad && crank == 0) *s8_fail = 1;
+        }
+        if (crank == 0) {
+          if (do_hi) exps[(int64_t)t * rows + row] = ch;
+          if (do_lo) exps[(int64_t)(n_hi + t) * rows + row] = cl;
+        }
+        *reinterpret_cast<float4*>(&s_prm[par][0]) = make_float4(sh, ih, 0.f, 0.f);
+        *reinterpret_cast<float4*>(&s_prm[par][4]) = make_float4(sl, il, 0.f, 0.f);
       }
-      if (tid == 0 && crank == 0) {
-        if (do_hi) exps[(int64_t)t * rows + row] = ch;
-        if (do_lo) exps[(int64_t)(n_hi + t) * rows + row] = cl;
-      }
+      __syncthreads();
+      const float4 ph = *reinterpret_cast<const float4*>(&s_prm[par][0]);
+      const float4 pl = *reinterpret_cast<const float4*>(&s_prm[par][4]);
       mh = 0.0f;
       ml = 0.0f;
-      const int64_t off_h = (int64_t)t * slice_stride + row * k_pad;
-      const int64_t off_l = (int64_t)(n_hi + t) * slice_stride + row * k_pad;
+      // A zero line has all residuals 0, so RN(r + sigma) - sigma is 0 there and
+      // the zero-line rule needs no select.
 #pragma unroll
-      for (int q = 0; q < NG; ++q) {
-        const int64_t k = kbase + 4 * ((int64_t)q * NT + tid);  // column in the row
+      for (int side = 0; side < 2; ++side) {
+        if (side == 0 ? !do_hi : !do_lo) continue;
+        const float sg = side == 0 ? ph.x : pl.x, iv = side == 0 ? ph.y : pl.y;
+        const uint32_t sg_bits = __float_as_uint(sg);
+        uint8_t* out = static_cast<uint8_t*>(slices_v) +
+                       ((int64_t)(side == 0 ? t : n_hi + t) * slice_stride + row * k_pad + kbase +
+                        4 * (int64_t)tid) * ESZ;
+        float mnext = 0.0f;
 #pragma unroll
-        for (int side = 0; side < 2; ++side) {
-          if (side == 0 ? !do_hi : !do_lo) continue;
-          const float sg = side == 0 ? sh : sl, iv = side == 0 ? ih : il;
-          const int zz = side == 0 ? zh : zl;
-          const uint32_t sg_bits = __float_as_uint(sg);
-          uint32_t w0 = 0, w1 = 0;
-          float mnext = 0.0f;
+        for (int q = 0; q < NG; ++q) {
+          uint32_t u[4];
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
             float& r = side == 0 ? rh[4 * q + h] : rl[4 * q + h];
             const float tt = __fadd_rn(r, sg);
-            const float v = zz ? 0.0f : __fsub_rn(tt, sg);
+            const float v = __fsub_rn(tt, sg);
             r = __fsub_rn(r, v);
             mnext = fmaxf(mnext, fabsf(r));
-            if constexpr (S8) {
-              // (columns >= K hold r = 0, so their code is 0)
-              w0 |= ((__float_as_uint(tt) - sg_bits) & 0xFFu) << (8 * h);
-            } else {
-              const uint32_t bits = bf16_bits_exact(__fmul_rn(v, iv));
-              if (h < 2) w0 |= bits << (16 * h);
-              else w1 |= bits << (16 * (h - 2));
+            if constexpr (S8) u[h] = __float_as_uint(tt) - sg_bits;  // the int8 code
+            else u[h] = __float_as_uint(__fmul_rn(v, iv));           // BF16 in the top half
+          }
+          if constexpr (!S8) {
+            // columns K..k_pad-1 are zeros even where 2^-c is not finite
+            const int64_t k = kbase + 4 * ((int64_t)q * NT + tid);
+            if (k + 3 >= K) {
+#pragma unroll
+              for (int h = 0; h < 4; ++h)
+                if (k + h >= K) u[h] = 0;
             }
           }
-          if (side == 0) mh = fmaxf(mh, mnext);
-          else ml = fmaxf(ml, mnext);
-          if (k < k_pad) {
-            const int64_t off = (side == 0 ? off_h : off_l) + k;
+          if (q < nq) {
             if constexpr (S8) {
-              *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(slices_v) + off) = w0;
+              const uint32_t w = __byte_perm(__byte_perm(u[0], u[1], 0x0040),
+                                             __byte_perm(u[2], u[3], 0x0040), 0x5410);
+              *reinterpret_cast<uint32_t*>(out + (int64_t)q * 4 * NT) = w;
             } else {
-              *reinterpret_cast<uint2*>(static_cast<uint16_t*>(slices_v) + off) = make_uint2(w0, w1);
+              *reinterpret_cast<uint2*>(out + (int64_t)q * 8 * NT) =
+                  make_uint2(__byte_perm(u[0], u[1], 0x7632), __byte_perm(u[2], u[3], 0x7632));
             }
           }
         }
+        if (side == 0) mh = mnext;
+        else ml = mnext;
       }
     }
-    if (S8 && bad && tid == 0 && crank == 0) *s8_fail = 1;
   }
   // Every issued copy lands before the CTA's shared memory is released.
   if (tid == 0) {

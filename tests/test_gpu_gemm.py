@@ -206,3 +206,28 @@ def test_accuracy_gate_256x8192x256(golden):
         err = float(np.linalg.norm(C.cpu().numpy() - R) / np.linalg.norm(R))
         ref = meta["ref_err_256x8192x256"][pname]["numpy"]
         assert err <= 1.5 * ref, (pname, err, ref)
+
+
+def test_wide_range_max_preset_config_c3():
+    """BASELINE config 3 in miniature: precision 'max' on (U(0,1)-0.5)*exp(10 N(0,1))
+    entries, K = 8192 (int8 codes, 256-wide tiles).  Per-row scaling truncates the
+    small entries of a row, so the reference's own error is large (about 1e-6);
+    'fused' must stay within 1.5x of the reference's matmul_numpy error against
+    the exact product, and 'ondevice' must be the reference's fused result bit
+    for bit."""
+    from ozaki_jax_b200.matmul import _ondevice_device
+    rng = np.random.RandomState(0)
+    n, k, m = 256, 8192, 256
+    A = (rng.rand(n, k) - 0.5) * np.exp(10 * rng.randn(n, k))
+    B = (rng.rand(k, m) - 0.5) * np.exp(10 * rng.randn(k, m))
+    E = O.exact_product(A, B)
+    ref_err = O.rel_err(O.ondevice_numpy(A, B, 5, 4), E)
+    Ad, Bd = torch.as_tensor(A).cuda(), torch.as_tensor(B).cuda()
+    C, st = _ondevice_device(Ad, Bd, 5, 4, "fused")
+    torch.cuda.synchronize()
+    assert st.item() == 0
+    err = O.rel_err(C.cpu().numpy(), E)
+    assert err <= 1.5 * ref_err, (err, ref_err)
+    C2, _ = _ondevice_device(Ad, Bd, 5, 4, "ondevice")
+    _, _, ref_fused = O.fused_ondevice(A, B, 5, 4)
+    assert same_bits(C2.cpu().numpy(), ref_fused)

@@ -178,6 +178,19 @@ int ozk_accumulate_2sum(const float* products, const int32_t* eA, const int32_t*
                         int64_t N, int64_t M, int n_hi, int n_lo, float* C_hi, float* C_lo,
                         double* C, int64_t ldc, void* stream);
 
+/* The general accumulate_2sum of the reference (accumulate_2sum with
+ * backend 'auto'/'jax'/'pallas', ozaki_jax/pallas_ops.py:372-396, arithmetic
+ * :178-239): products [n_products][N][M] FP32, col_scales [n_products][M]
+ * FP32, row_scales [n_groups][N] FP32, all on the device; the block structure
+ * block_group_sizes as HOST arrays: group_sizes[g] products per group, and
+ * block_ends[b] = one past the last group of block b (n_blocks <= 8).
+ * Writes C_hi, C_lo (FP32 [N][M], either may be NULL), bit-identical to the
+ * reference. */
+int ozk_accumulate_2sum_scaled(const float* products, const float* col_scales,
+                               const float* row_scales, const int32_t* group_sizes, int n_groups,
+                               const int32_t* block_ends, int n_blocks, int64_t N, int64_t M,
+                               float* C_hi, float* C_lo, void* stream);
+
 /* ---------------------------------------------------------------- pipelines */
 
 /* Workspace bytes ozk_matmul_f64 uses for an N x K by K x M product with

@@ -9,17 +9,22 @@ There is no CPU fallback: without a CUDA device or the library, calls raise.
 
 __version__ = "0.1.0"
 
-from .matmul import matmul, compute_rho_f32, compute_rho_f64, ondevice_safety_report
+from .matmul import (matmul, matmul_numpy, compute_rho_f32, compute_rho_f64,
+                     ondevice_safety_report)
 from .gram import gram
 from .solve import residual
 from .extract import (
+    extract_split_rows, extract_split_cols,
     f32_extract_split_rows, f32_extract_split_cols,
     jax_extract_split_rows, jax_extract_split_cols,
 )
+from .accum import accumulate_2sum, validate_accumulation_2sum
 
 __all__ = [
-    "matmul", "gram", "residual",
+    "matmul", "matmul_numpy", "gram", "residual",
+    "extract_split_rows", "extract_split_cols",
     "f32_extract_split_rows", "f32_extract_split_cols",
     "jax_extract_split_rows", "jax_extract_split_cols",
+    "accumulate_2sum", "validate_accumulation_2sum",
     "compute_rho_f32", "compute_rho_f64", "ondevice_safety_report",
 ]

@@ -61,6 +61,8 @@ SIGNATURES = {
                                   vp, vp]),
     "ozk_accumulate_2sum": (c_int, [vp, vp, vp, c_i64, c_i64, c_int, c_int, vp, vp, vp, c_i64,
                                     vp]),
+    "ozk_accumulate_2sum_scaled": (c_int, [vp, vp, vp, vp, c_int, vp, c_int, c_i64, c_i64, vp, vp,
+                                           vp]),
     "ozk_matmul_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_int, c_int]),
     "ozk_matmul_f64": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64, c_int, c_int,
                                c_int, c_int, vp, c_size, vp, vp]),

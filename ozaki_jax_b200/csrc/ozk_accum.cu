@@ -68,6 +68,88 @@ __global__ void k_accumulate_2sum(const float* __restrict__ products, const int3
   }
 }
 
+// The general form of the reference's accumulate_2sum (pallas_ops.py:178-239,
+// :372-396): caller-given FP32 scales and block/group structure.  Block b
+// holds groups [block_end[b-1], block_end[b]); group g consumes group_size[g]
+// products in order, each times its column scale, then both words times the
+// group's row scale.
+struct GroupSpec {
+  int16_t size[OZK_MAX_PAIRS];
+  int16_t block_end[8];
+  int n_groups;
+  int n_blocks;
+};
+
+__global__ void k_accumulate_2sum_scaled(const float* __restrict__ products,
+                                         const float* __restrict__ col_scales,
+                                         const float* __restrict__ row_scales,
+                                         const __grid_constant__ GroupSpec spec, int64_t N,
+                                         int64_t M, float* C_hi, float* C_lo) {
+  const int64_t plane = N * M;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < plane;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / M, c = idx % M;
+    int64_t p = 0;
+    int g = 0;
+    float blo[8];
+    TwoSum out{0.0f, 0.0f};
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      blo[b] = 0.0f;
+      if (b >= spec.n_blocks) continue;
+      TwoSum blk{0.0f, 0.0f};
+      for (; g < spec.block_end[b]; ++g) {
+        TwoSum in{0.0f, 0.0f};
+        for (int j = 0; j < spec.size[g]; ++j, ++p)
+          in.add(__fmul_rn(products[p * plane + idx], col_scales[p * M + c]));
+        const float rs = row_scales[(int64_t)g * N + r];
+        blk.add(__fmul_rn(in.hi, rs));
+        blk.add(__fmul_rn(in.lo, rs));
+      }
+      out.add(blk.hi);  // block hi words in block order ...
+      blo[b] = blk.lo;
+    }
+#pragma unroll
+    for (int b = 0; b < 8; ++b)  // ... then the lo words
+      if (b < spec.n_blocks) out.add(blo[b]);
+    if (C_hi) C_hi[idx] = out.hi;
+    if (C_lo) C_lo[idx] = out.lo;
+  }
+}
+
+int launch_accumulate_2sum_scaled(const float* products, const float* col_scales,
+                                  const float* row_scales, const int32_t* group_sizes,
+                                  int n_groups, const int32_t* block_ends, int n_blocks, int64_t N,
+                                  int64_t M, float* C_hi, float* C_lo, cudaStream_t stream) {
+  if (n_groups < 1 || n_groups > OZK_MAX_PAIRS || n_blocks < 1 || n_blocks > 8)
+    return set_error(OZK_ERR_ARG, "accumulate_2sum: 1..%d groups in 1..8 blocks", OZK_MAX_PAIRS);
+  GroupSpec spec;
+  int prev = 0;
+  for (int b = 0; b < n_blocks; ++b) {
+    if (block_ends[b] < prev || block_ends[b] > n_groups)
+      return set_error(OZK_ERR_ARG, "accumulate_2sum: bad block boundaries");
+    spec.block_end[b] = (int16_t)(prev = block_ends[b]);
+  }
+  if (prev != n_groups) return set_error(OZK_ERR_ARG, "accumulate_2sum: blocks do not cover the groups");
+  for (int g = 0; g < n_groups; ++g) {
+    if (group_sizes[g] < 0 || group_sizes[g] > OZK_MAX_PAIRS)
+      return set_error(OZK_ERR_ARG, "accumulate_2sum: bad group size");
+    spec.size[g] = (int16_t)group_sizes[g];
+  }
+  spec.n_groups = n_groups;
+  spec.n_blocks = n_blocks;
+  const int64_t plane = N * M;
+  if (plane == 0) return OZK_OK;
+  int dev;
+  cudaGetDevice(&dev);
+  int64_t blocks = (plane + 255) / 256;
+  int64_t cap = (int64_t)device_sm_count(dev) * 8;
+  k_accumulate_2sum_scaled<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, stream>>>(
+      products, col_scales, row_scales, spec, N, M, C_hi, C_lo);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OZK_OK : set_cuda_error("k_accumulate_2sum_scaled launch", e);
+}
+
 int launch_accumulate_2sum(const float* products, const int32_t* eA, const int32_t* eB, int64_t N,
                            int64_t M, int n_hi, int n_lo, float* C_hi, float* C_lo, double* C,
                            int64_t ldc, cudaStream_t stream) {

@@ -508,6 +508,18 @@ int ozk_accumulate_2sum(const float* products, const int32_t* eA, const int32_t*
                                 (cudaStream_t)stream);
 }
 
+int ozk_accumulate_2sum_scaled(const float* products, const float* col_scales,
+                               const float* row_scales, const int32_t* group_sizes, int n_groups,
+                               const int32_t* block_ends, int n_blocks, int64_t N, int64_t M,
+                               float* C_hi, float* C_lo, void* stream) {
+  if (!products || !col_scales || !row_scales || !group_sizes || !block_ends)
+    return set_error(OZK_ERR_ARG, "NULL pointer");
+  if (N < 0 || M < 0) return set_error(OZK_ERR_ARG, "bad shape");
+  return launch_accumulate_2sum_scaled(products, col_scales, row_scales, group_sizes, n_groups,
+                                       block_ends, n_blocks, N, M, C_hi, C_lo,
+                                       (cudaStream_t)stream);
+}
+
 size_t ozk_matmul_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo) {
   return layout(nullptr, N, K, M, n_hi + n_lo, 0, M * K, cur_state_bytes()).bytes;
 }

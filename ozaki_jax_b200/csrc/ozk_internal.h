@@ -103,6 +103,10 @@ size_t gemm_state_bytes(int dev);
 // Smallest workspace ozk_matmul_f64 (OZK_ACC_F64) accepts: without the state
 // scratch it runs 128-wide tiles.
 size_t matmul_min_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi, int n_lo);
+int launch_accumulate_2sum_scaled(const float* products, const float* col_scales,
+                                  const float* row_scales, const int32_t* group_sizes,
+                                  int n_groups, const int32_t* block_ends, int n_blocks, int64_t N,
+                                  int64_t M, float* C_hi, float* C_lo, cudaStream_t stream);
 int launch_accumulate_2sum(const float* products, const int32_t* eA, const int32_t* eB, int64_t N,
                            int64_t M, int n_hi, int n_lo, float* C_hi, float* C_lo, double* C,
                            int64_t ldc, cudaStream_t stream);

@@ -95,3 +95,52 @@ def jax_extract_split_rows(X_f32, rho, n_slices=5):
 def jax_extract_split_cols(X_f32, rho, n_slices=5):
     """Stacked variant: ((n_slices, K, M) slices, (n_slices, M) exponents)."""
     return _extract_f32(X_f32, rho, n_slices, 0)
+
+
+def _extract_f64(X_f64, rho, n_slices, axis):
+    """FP64 sigma-trick extraction of the host pipeline on the device:
+    (slices (n, lines, K) FP32, exponents (n, lines) FP64)."""
+    n_slices = int(n_slices)
+    if n_slices < 1:
+        raise ValueError("n_slices must be >= 1")
+    lib = L.load()
+    dev = D.device_of(X_f64)
+    Xd = D.to_device_f64(X_f64, dev)
+    if Xd.dim() != 2:
+        raise ValueError("X must be 2D")
+    lines, K = (Xd.shape if axis == 1 else Xd.shape[::-1])
+    k_pad = (max(K, 1) + 63) // 64 * 64
+    slices = torch.empty((n_slices, lines, k_pad), dtype=torch.int16, device=dev)
+    exps = torch.empty((n_slices, lines), dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    if lines > 0 and K > 0:
+        fn = lib.ozk_extract_rows_host_f64 if axis == 1 else lib.ozk_extract_cols_host_f64
+        L.check(fn(Xd.data_ptr(), Xd.stride(0), *((lines, K) if axis == 1 else (K, lines)),
+                   int(rho), n_slices, slices.data_ptr(), k_pad, exps.data_ptr(),
+                   status.data_ptr(), D.stream_handle(dev)))
+    S = _bf16_to_f32(slices[:, :, :K])
+    if axis == 0:
+        S = S.transpose(1, 2)
+    return S.contiguous(), exps.to(torch.float64)
+
+
+def _as_lists(S, E, device_in):
+    if device_in:
+        return list(S), list(E)
+    S, E = S.cpu().numpy(), E.cpu().numpy()
+    return [S[i] for i in range(len(S))], [E[i] for i in range(len(E))]
+
+
+def extract_split_rows(X_f64, rho, n_slices=8):
+    """Row-scaled FP64 sigma-trick slices of the host pipeline
+    (extract_split_rows, ozaki_jax/extract.py:21-65): (list of FP32 slices
+    (N, K), list of FP64 exponent vectors (N,)), NumPy in -> NumPy out."""
+    S, E = _extract_f64(X_f64, rho, n_slices, 1)
+    return _as_lists(S, E, D.is_device_array(X_f64))
+
+
+def extract_split_cols(X_f64, rho, n_slices=8):
+    """Column-scaled FP64 slices (extract_split_cols, ozaki_jax/extract.py:68-103):
+    (list of FP32 slices (K, M), list of FP64 exponent vectors (M,))."""
+    S, E = _extract_f64(X_f64, rho, n_slices, 0)
+    return _as_lists(S, E, D.is_device_array(X_f64))

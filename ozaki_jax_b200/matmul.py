@@ -272,3 +272,25 @@ def matmul(A, B, n_slices=8, safe_mode="raise", pipeline="host",
     if input_is_device or isinstance(C, np.ndarray):
         return C
     return D.to_host_f64(C)
+
+
+def matmul_numpy(A_f64, B_f64, n_slices=8, safe_mode="raise", pipeline="host",
+                 precision="high"):
+    """The reference's NumPy pipeline (matmul_numpy, ozaki_jax/matmul.py:854-895) with
+    its semantics, computed on the device; always returns a NumPy array.
+
+    pipeline='ondevice': FP32 double split, BF16 slices, exact products summed in
+    FP64 (the reference's _accumulate_block_products) -> accumulation='host'.
+    pipeline='host': FP64 slices with triangular pairs (matmul(pipeline='host')).
+    """
+    A = np.asarray(A_f64, dtype=np.float64)
+    B = np.asarray(B_f64, dtype=np.float64)
+    if pipeline == "ondevice":
+        n_hi, n_lo = _resolve_precision(precision)
+        C = _matmul_ondevice(A, B, safe_mode, "host", n_hi, n_lo)
+    elif pipeline == "host":
+        from .host import matmul_host
+        C = matmul_host(A, B, n_slices, safe_mode)
+    else:
+        raise ValueError(f"Unknown pipeline={pipeline!r}; expected 'host' or 'ondevice'.")
+    return C if isinstance(C, np.ndarray) else D.to_host_f64(C)

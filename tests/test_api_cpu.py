@@ -57,3 +57,22 @@ def test_preflight_bound_reasons():
     # host pipeline: K=10000 with 8 slices is unsafe (ci_cpu_validate.py:108-111)
     rho, reasons = host_safety_reasons(10000, 8)
     assert reasons == ["insufficient slice budget: n_slices*bits_per_slice=40 < 53"]
+
+
+def test_accumulate_2sum_backend_text_without_gpu():
+    """The reference's backend error text, raised before any device work."""
+    import numpy as np
+    import ozaki_jax_b200 as oz
+    with pytest.raises(ValueError) as ei:
+        oz.accumulate_2sum(np.zeros((1, 2, 2), np.float32), np.ones((1, 2), np.float32),
+                           np.ones((1, 2), np.float32), ((1,),), backend="xla")
+    assert str(ei.value) == "Unknown backend='xla'; expected 'auto', 'jax', or 'pallas'."
+
+
+def test_public_names_match_the_reference_hot_path():
+    import ozaki_jax_b200 as oz
+    for name in ("matmul", "matmul_numpy", "gram", "residual", "extract_split_rows",
+                 "extract_split_cols", "f32_extract_split_rows", "f32_extract_split_cols",
+                 "jax_extract_split_rows", "jax_extract_split_cols", "accumulate_2sum",
+                 "validate_accumulation_2sum"):
+        assert callable(getattr(oz, name)), name

@@ -321,15 +321,21 @@ def ours(args):
     pinB = torch.empty(B.shape, dtype=torch.float64, pin_memory=True)
     pinB.numpy()[...] = B
     hA, hB = pinA.numpy(), pinB.numpy()
+    if world == 1:
+        e2e_call = lambda: oz.matmul(hA, hB, pipeline="ondevice", precision=args.precision)
+    else:
+        # each rank uploads its rows of A and 1/P of B; B is all-gathered over NCCL
+        from ozaki_jax_b200.distributed import matmul_rowsharded_host
+        e2e_call = lambda: matmul_rowsharded_host(hA, hB, precision=args.precision)
     # two warm-up calls: the result of one call is still alive while the next
     # runs, so torch's pinned-host pool needs two output buffers
-    Ch = oz.matmul(hA, hB, pipeline="ondevice", precision=args.precision)
-    Ch = oz.matmul(hA, hB, pipeline="ondevice", precision=args.precision)
+    Ch = e2e_call()
+    Ch = e2e_call()
     barrier()
     e2e_steps = max(1, min(args.steps, 3))
     e0.record(stream)
     for _ in range(e2e_steps):
-        Ch = oz.matmul(hA, hB, pipeline="ondevice", precision=args.precision)
+        Ch = e2e_call()
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
@@ -382,9 +388,12 @@ def ours(args):
                              "kind": "port",
                              "sample": f"first {cpu_rows} rows of A x full B ({cpu_dt:.1f} s), "
                                        f"NumPy oracle, OpenBLAS threads = cores"},
+            # copies of the whole job (all ranks): A and C once, B once in total
+            # (world == 1) or in per-rank shares padded to ceil(K/P) rows
             "e2e": {"value": flops_fp64eq / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": int(8 * (nb * k + k * m)),
-                    "d2h_bytes_per_step": int(8 * nb * m)},
+                    "h2d_bytes_per_step": int(8 * (n * k + (k * m if world == 1 else
+                                                            world * ((k + world - 1) // world) * m))),
+                    "d2h_bytes_per_step": int(8 * n * m)},
             "clocks": clk,
             "gpu_launches": 4 * args.steps,
         }

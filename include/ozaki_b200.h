@@ -218,7 +218,8 @@ int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, d
  * where the arrays are transferred to the device, the jitted pipeline runs and
  * the result comes back to the host): A, B, C are host pointers (pinned memory
  * copies at full DMA speed; pageable memory works through the driver's
- * staging).  The copies overlap the compute: B is copied and column-extracted
+ * staging); any of them may also be device memory of this GPU (unified
+ * addressing picks the copy direction).  The copies overlap the compute: B is copied and column-extracted
  * first, then A and C move in row blocks of block_rows rows (0 = automatic) on
  * two internal copy streams while the previous block's slice GEMM runs on
  * `stream`.  Blocking: returns after C is written; *status_host receives the

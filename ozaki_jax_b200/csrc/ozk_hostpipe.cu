@@ -13,7 +13,9 @@
 // GEMM produces exactly the rows of C the full product would (same slices, same
 // exponents, same per-element sums), so the result does not depend on the
 // blocking.  Events order the three streams; nothing here synchronises the
-// host until the last copy has been issued.
+// host until the last copy has been issued.  The copies use unified
+// addressing, so any of A, B and C may also be device memory (a B already
+// gathered on this GPU is copied on the device, not over PCIe).
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -232,13 +234,13 @@ extern "C" int ozk_matmul_f64_hostbuf(const double* A, int64_t lda, const double
 
   // Host -> device: B, then the row blocks of A.
   OZK_TRY_CUDA(cudaMemcpy2DAsync(w.B, (size_t)M * 8, B, (size_t)ldb * 8, (size_t)M * 8, (size_t)K,
-                                 cudaMemcpyHostToDevice, cs.h2d),
+                                 cudaMemcpyDefault, cs.h2d),
                "cudaMemcpy2DAsync(B)");
   OZK_TRY_CUDA(cudaEventRecord(ev_b, cs.h2d), "cudaEventRecord");
   for (int b = 0; b < nblk; ++b) {
     const int64_t r0 = b * br, nb = (r0 + br <= N ? br : N - r0);
     OZK_TRY_CUDA(cudaMemcpy2DAsync(w.A + r0 * K, (size_t)K * 8, A + r0 * lda, (size_t)lda * 8,
-                                   (size_t)K * 8, (size_t)nb, cudaMemcpyHostToDevice, cs.h2d),
+                                   (size_t)K * 8, (size_t)nb, cudaMemcpyDefault, cs.h2d),
                  "cudaMemcpy2DAsync(A)");
     OZK_TRY_CUDA(cudaEventRecord(ev_a[b], cs.h2d), "cudaEventRecord");
   }
@@ -301,7 +303,7 @@ extern "C" int ozk_matmul_f64_hostbuf(const double* A, int64_t lda, const double
     const int64_t r0 = b * br, nb = (r0 + br <= N ? br : N - r0);
     OZK_TRY_CUDA(cudaStreamWaitEvent(cs.d2h, ev_c[b], 0), "cudaStreamWaitEvent");
     OZK_TRY_CUDA(cudaMemcpy2DAsync(C + r0 * ldc, (size_t)ldc * 8, w.C + r0 * M, (size_t)M * 8,
-                                   (size_t)M * 8, (size_t)nb, cudaMemcpyDeviceToHost, cs.d2h),
+                                   (size_t)M * 8, (size_t)nb, cudaMemcpyDefault, cs.d2h),
                  "cudaMemcpy2DAsync(C)");
   }
 

@@ -18,6 +18,7 @@ CPU); the compute is libozaki_b200.
 
 import ctypes
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -167,3 +168,65 @@ def matmul_rowsharded(A_local, B, K=None, precision="high", b_source="replicated
                          if flags & (L.OZK_FLAG_NONFINITE | L.OZK_FLAG_RANGE)
                          else f"device status {flags}")
     return C
+
+
+def matmul_rowsharded_host(A_local, B, precision="high", group=None):
+    """This rank's rows of C = A @ B from host arrays, with B's upload split over
+    the ranks.
+
+    A_local: this rank's row block of A (NumPy, host).  B: the K x M matrix as a
+    host array on every rank; rank r uploads only its share of B's rows
+    (rows [r*ceil(K/P), (r+1)*ceil(K/P)) ), the shares are all-gathered over
+    NCCL (NVLink) into the full B on every GPU, and the on-device pipeline runs
+    on this rank's rows.  Each rank moves its A rows, 1/P of B and its C rows
+    over PCIe instead of all of B.  Returns this rank's rows of C as NumPy,
+    bit-identical to the same rows of the single-GPU result.  All ranks must
+    call it.
+    """
+    from .matmul import _flags_reasons, _PREFIX
+    n_hi, n_lo = _resolve_precision(precision)
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    A = np.ascontiguousarray(A_local, dtype=np.float64)
+    Bh = np.asarray(B, dtype=np.float64)
+    if A.ndim != 2 or Bh.ndim != 2 or A.shape[1] != Bh.shape[0]:
+        raise ValueError(f"Incompatible shapes for matmul: {A.shape} and {Bh.shape}.")
+    K, M = Bh.shape
+    kc = (K + world - 1) // world
+    k0, k1 = min(K, rank * kc), min(K, (rank + 1) * kc)
+    share = torch.zeros((kc, M), dtype=torch.float64, device=dev)
+    if k1 > k0:
+        share[: k1 - k0].copy_(D.to_device_f64(Bh[k0:k1], dev))
+    gathered = torch.empty((world * kc, M), dtype=torch.float64, device=dev)
+    dist.all_gather_into_tensor(gathered, share, group=group)
+    Bd = gathered[:K]
+    nb = A.shape[0]
+    if nb == 0 or M == 0:
+        return np.zeros((nb, M))
+    # A and C stay on the host: the host-buffer pipeline streams them in row
+    # blocks over PCIe while the blocks before are computed; B is read from
+    # this GPU's gathered copy.
+    lib = L.load()
+    Ch = D.host_empty_f64((nb, M))
+    ws_bytes = lib.ozk_matmul_hostbuf_workspace_bytes(nb, K, M, n_hi, n_lo, L.OZK_ACC_FIXED, 0)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    flags = ctypes.c_int32(0)
+    L.check(lib.ozk_matmul_f64_hostbuf(
+        A.ctypes.data, K, Bd.data_ptr(), M, Ch.ctypes.data, M, nb, K, M, compute_rho_f32(K),
+        n_hi, n_lo, L.OZK_ACC_FIXED, 0, ws.data_ptr(), ws_bytes, ctypes.byref(flags),
+        D.stream_handle(dev)))
+    if flags.value & L.OZK_FLAG_TIMEOUT:
+        raise L.OzakiError(L.OZK_ERR_TIMEOUT, "a device-side wait exceeded its time budget")
+    if flags.value:
+        raise ValueError(_PREFIX + "; ".join(_flags_reasons(flags.value)))
+    return Ch
+
+
+def residual_rowsharded(A_local, x, b_local, precision="high", accumulation="bf16_interleaved"):
+    """This rank's rows of r = b - A x (residual(mode='ozaki')): rows of A and b
+    are independent and x is given to every rank, so there is no collective;
+    the result equals the same rows of the single-GPU residual bit for bit."""
+    from .solve import residual
+    return residual(A_local, x, b_local, precision=precision, accumulation=accumulation,
+                    mode="ozaki")

@@ -35,7 +35,9 @@ def _worker(rank, world, port, q):
                             timeout=timedelta(seconds=120))
     try:
         import ozaki_jax_b200 as oz
-        from ozaki_jax_b200.distributed import gather_rows, matmul_rowsharded, row_range
+        from ozaki_jax_b200.distributed import (gather_rows, matmul_rowsharded,
+                                                matmul_rowsharded_host, residual_rowsharded,
+                                                row_range)
         rng = np.random.RandomState(0)
         out = {}
         # K = 700: BF16 slices; K = 5000 (rho 19, 600 rows per rank): int8 codes
@@ -49,6 +51,16 @@ def _worker(rank, world, port, q):
                 C = matmul_rowsharded(Ad, Bd, b_source=src)
                 full = gather_rows(C, n)
                 out[(k, src)] = bool(np.array_equal(full.cpu().numpy(), ref))
+            # host arrays, B uploaded in shares and all-gathered over NCCL
+            Ch = matmul_rowsharded_host(A[r0:r1], B)
+            out[(k, "host")] = bool(np.array_equal(Ch, ref[r0:r1]))
+        # residual rows: no collective, the single-GPU rows bit for bit
+        A = rng.randn(1000, 5000)
+        X, Bv = rng.randn(5000, 16), rng.randn(1000, 16)
+        ref = oz.residual(A, X, Bv, mode="ozaki")
+        r0, r1 = row_range(1000, rank, world)
+        out["residual"] = bool(np.array_equal(residual_rowsharded(A[r0:r1], X, Bv[r0:r1]),
+                                              ref[r0:r1]))
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
@@ -75,4 +87,4 @@ def test_rowsharded_matmul_two_gpus():
         p.join(timeout=120)
         assert p.exitcode == 0
     for _, out in res:
-        assert len(out) == 4 and all(out.values()), out
+        assert len(out) == 7 and all(out.values()), out

@@ -230,3 +230,112 @@ def residual_rowsharded(A_local, x, b_local, precision="high", accumulation="bf1
     from .solve import residual
     return residual(A_local, x, b_local, precision=precision, accumulation=accumulation,
                     mode="ozaki")
+
+
+def gram_rowsharded(A_local, precision="high", group=None):
+    """This rank's block of rows of G = A^T A (gram(mode='ozaki')) with A's rows
+    split over the ranks.
+
+    A_local: this rank's rows of A (CUDA float64, N_r x K).  Rank r owns columns
+    [rK/P, (r+1)K/P) of A and rows [rK/P, (r+1)K/P) of G:
+      1. an all-to-all over NCCL gives each rank every row of its columns, so it
+         extracts their slices (lines of length N) itself, as the single-GPU
+         gram does;
+      2. the slice stacks and exponents are all-gathered;
+      3. each rank multiplies its lines' slices by all of them: its rows of G.
+    Pair (a, b) of element (j, i) is pair (b, a) of element (i, j), and the pair
+    set and the fixed-point term scaling are symmetric under that swap, so the
+    rows equal the single-GPU symmetric gram bit for bit.  Returns this rank's
+    rows of G (CUDA float64, K_r x K).  All ranks must call it.
+    """
+    from .matmul import _flags_reasons, _PREFIX
+    lib = L.load()
+    n_hi, n_lo = _resolve_precision(precision)
+    nS = n_hi + n_lo
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    Ad = A_local.to(dtype=torch.float64).contiguous()
+    dev = Ad.device
+    n_loc, K = Ad.shape
+    counts = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(world)]
+    dist.all_gather(counts, torch.tensor([n_loc], dtype=torch.int64, device=dev), group=group)
+    counts = [int(c.item()) for c in counts]
+    N = sum(counts)
+    cols = [row_range(K, r, world) for r in range(world)]
+    c0, c1 = cols[rank]
+    kr = c1 - c0
+    # 1. columns of A to their owners
+    send = torch.cat([Ad[:, a:b].reshape(-1) for a, b in cols])
+    recv = torch.empty(N * kr, dtype=torch.float64, device=dev)
+    dist.all_to_all_single(recv, send, output_split_sizes=[n * kr for n in counts],
+                           input_split_sizes=[n_loc * (b - a) for a, b in cols], group=group)
+    A_cols = torch.cat([blk.view(n, kr) for blk, n in zip(recv.split([n * kr for n in counts]),
+                                                          counts)])  # N x kr
+    rho = compute_rho_f32(N)
+    kmax = max(b - a for a, b in cols)
+    # the slice format is decided the same way on every rank
+    use_s8 = rho >= 19 and min(b - a for a, b in cols) >= 256 and K >= 256 and N <= 65536
+    sh = D.stream_handle(dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    pa = (ctypes.c_uint8 * 256)()
+    pb = (ctypes.c_uint8 * 256)()
+    npairs = L.check(lib.ozk_pair_schedule_snake(n_hi, n_lo, pa, pb, 256))
+    GW = torch.empty(lib.ozk_slice_gemm_workspace_bytes(), dtype=torch.uint8, device=dev)
+    BT = torch.empty(max(kr * N, 1), dtype=torch.float64, device=dev)
+    G = torch.empty((kr, K), dtype=torch.float64, device=dev)
+
+    def slices_and_gemm(s8):
+        n_pad = (N + 127) // 128 * 128 if s8 else (N + 63) // 64 * 64
+        dt = torch.int8 if s8 else torch.int16
+        S = torch.zeros((nS, kmax, n_pad), dtype=dt, device=dev)
+        E = torch.zeros((nS, kmax), dtype=torch.int32, device=dev)
+        fail = torch.zeros(1, dtype=torch.int32, device=dev)
+        # this rank's lines: slices [nS][kr][n_pad], padded to kmax lines for the gather
+        Sk = torch.empty((nS, kr, n_pad), dtype=dt, device=dev)
+        Ek = torch.empty((nS, kr), dtype=torch.int32, device=dev)
+        if kr > 0:
+            if s8:
+                L.check(lib.ozk_extract_cols_s8_f64(
+                    A_cols.data_ptr(), kr, N, kr, rho, n_hi, n_lo, Sk.data_ptr(), n_pad,
+                    Ek.data_ptr(), BT.data_ptr(), BT.numel() * 8, fail.data_ptr(),
+                    status.data_ptr(), sh))
+            else:
+                L.check(lib.ozk_extract_cols_f64(
+                    A_cols.data_ptr(), kr, N, kr, rho, n_hi, n_lo, Sk.data_ptr(), n_pad,
+                    Ek.data_ptr(), BT.data_ptr(), BT.numel() * 8, status.data_ptr(), sh))
+            S[:, :kr] = Sk
+            E[:, :kr] = Ek
+        if s8:
+            # a code without an exact int8 value on any rank sends every rank to BF16
+            dist.all_reduce(fail, op=dist.ReduceOp.MAX, group=group)
+            if int(fail.item()):
+                return False
+        # 2. every rank's slices: [P][nS][kmax][n_pad] -> [nS][K][n_pad]
+        allS = torch.empty((world,) + tuple(S.shape), dtype=dt, device=dev)
+        allE = torch.empty((world,) + tuple(E.shape), dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(allS.view(torch.uint8), S.view(torch.uint8), group=group)
+        dist.all_gather_into_tensor(allE, E, group=group)
+        SB = torch.cat([allS[r, :, : b - a] for r, (a, b) in enumerate(cols)], dim=1).contiguous()
+        EB = torch.cat([allE[r, :, : b - a] for r, (a, b) in enumerate(cols)], dim=1).contiguous()
+        if kr == 0:
+            return True
+        # 3. this rank's rows of G
+        if s8:
+            L.check(lib.ozk_slice_gemm_s8(Sk.data_ptr(), Ek.data_ptr(), nS, SB.data_ptr(),
+                                          EB.data_ptr(), nS, kr, K, n_pad, pa, pb, npairs, 0, 1.0,
+                                          0.0, None, 0, G.data_ptr(), K, GW.data_ptr(), GW.numel(),
+                                          rho, None, status.data_ptr(), sh))
+        else:
+            L.check(lib.ozk_slice_gemm(Sk.data_ptr(), Ek.data_ptr(), nS, SB.data_ptr(),
+                                       EB.data_ptr(), nS, kr, K, n_pad, pa, pb, npairs,
+                                       L.OZK_ACC_FIXED, 0, 1.0, 0.0, None, 0, G.data_ptr(), K,
+                                       None, GW.data_ptr(), GW.numel(), rho, status.data_ptr(),
+                                       sh))
+        return True
+
+    if not (use_s8 and slices_and_gemm(True)):
+        slices_and_gemm(False)
+    flags = int(status.item())
+    if flags:
+        raise ValueError(_PREFIX + "; ".join(_flags_reasons(flags)))
+    return G

@@ -35,7 +35,7 @@ def _worker(rank, world, port, q):
                             timeout=timedelta(seconds=120))
     try:
         import ozaki_jax_b200 as oz
-        from ozaki_jax_b200.distributed import (gather_rows, matmul_rowsharded,
+        from ozaki_jax_b200.distributed import (gather_rows, gram_rowsharded, matmul_rowsharded,
                                                 matmul_rowsharded_host, residual_rowsharded,
                                                 row_range)
         rng = np.random.RandomState(0)
@@ -61,6 +61,15 @@ def _worker(rank, world, port, q):
         r0, r1 = row_range(1000, rank, world)
         out["residual"] = bool(np.array_equal(residual_rowsharded(A[r0:r1], X, Bv[r0:r1]),
                                               ref[r0:r1]))
+        # gram with A's rows split: N = 3000 (BF16 slices), N = 6000 (int8 codes);
+        # this rank's rows of G equal the single-GPU gram's bit for bit
+        for n, k in ((3000, 300), (6000, 700)):
+            A = rng.randn(n, k) * np.exp(rng.randn(1, k))
+            ref = oz.gram(A, mode="ozaki")
+            r0, r1 = row_range(n, rank, world)
+            Gr = gram_rowsharded(torch.as_tensor(A[r0:r1]).to(dev))
+            c0, c1 = row_range(k, rank, world)
+            out[("gram", n)] = bool(np.array_equal(Gr.cpu().numpy(), ref[c0:c1]))
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
@@ -87,4 +96,4 @@ def test_rowsharded_matmul_two_gpus():
         p.join(timeout=120)
         assert p.exitcode == 0
     for _, out in res:
-        assert len(out) == 7 and all(out.values()), out
+        assert len(out) == 9 and all(out.values()), out

@@ -369,6 +369,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
     uint32_t acc_it = 0;
     bool ok = true;
     long long ep_wait = 0, ep_busy = 0, ep_pairs = 0;
+    long long Sa[16], Sb[16];  // running sums of two column chunks (int8 wide tiles)
     for (int t = unit; ok && t < g.num_tiles; t += n_units) {
       int tm, tn;
       tile_coords(g, t, tm, tn);
@@ -404,6 +405,77 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
         const uint32_t t_acc = tmem + lane_base + buf * BN;
         const uint32_t t_lo = tmem + lane_base + 2 * BN;
         const uint32_t t_hi = tmem + lane_base + 3 * BN;
+        if constexpr (S8 && Cfg::GSTATE) {
+          // int8 codes, fixed-point sums, running sums in the L2 scratch.  The
+          // columns go in chunks of 16 with the next chunk's running sums in
+          // flight while this one is computed, and chunk 0 of the next pair is
+          // requested before this warp waits for that pair's accumulator.
+          constexpr int C2 = 16;
+          constexpr int NCH = Cfg::EPI_COLS / C2;
+          const int ta = ea - eA0 + kFixFrac;
+          auto load_state = [&](long long (&S)[C2], int c0) {
+#pragma unroll
+            for (int j = 0; j < C2; ++j)
+              S[j] = ld_l2_hint((const long long*)(gst + (int64_t)(c0 + j) * kBM), l2keep);
+          };
+          auto process = [&](const long long (&S)[C2], int c0) {
+            uint32_t P[C2];
+            tmem_ld16(t_acc + c0, P);
+            tmem_wait_ld();
+            long long acc[C2];
+#pragma unroll
+            for (int j = 0; j < C2; ++j) {
+              const int db = b == 0 ? 0 : s_eB[b * BN + c0 + j];  // eb - eB0
+              acc[j] = fixed_term_s32((int32_t)P[j], ta + db) + (first ? 0ll : S[j]);
+            }
+            if (!last) {
+#pragma unroll
+              for (int j = 0; j < C2; ++j)
+                st_l2_hint((long long*)(gst + (int64_t)(c0 + j) * kBM), acc[j], l2keep);
+              return;
+            }
+            if (!rvalid) return;
+            double V[C2];
+#pragma unroll
+            for (int j = 0; j < C2; ++j) {
+              double v = g.alpha * fixed_value(acc[j], eA0 + s_eB[c0 + j] + g.fix_scale);
+              if (g.beta != 0.0 && col0 + c0 + j < g.M)
+                v = fma(g.beta, g.Cin[row * g.ldcin + col0 + c0 + j], v);
+              V[j] = v;
+            }
+            const int64_t cb = col0 + c0;
+            double* crow = g.C + row * g.ldc + cb;
+            if (!g.symmetric && g.c_vec && cb + C2 <= g.M) {
+#pragma unroll
+              for (int j = 0; j < C2; j += 4) st_global_v4_f64(crow + j, V[j], V[j + 1], V[j + 2], V[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < C2; ++j) {
+                const int64_t col = cb + j;
+                if (col < g.M) {
+                  if (!g.symmetric) {
+                    crow[j] = V[j];
+                  } else if (tm != tn || col >= row) {
+                    crow[j] = V[j];
+                    g.C[col * g.ldc + row] = V[j];
+                  }
+                }
+              }
+            }
+          };
+          // Sa holds chunk 0 of this pair when it is not the first (loaded at
+          // the end of the previous pair); chunks alternate between Sa and Sb.
+#pragma unroll 1
+          for (int ci = 0; ci < NCH; ci += 2) {
+            const int c0 = cbeg + ci * C2;
+            if (!first) load_state(Sb, c0 + C2);
+            process(Sa, c0);
+            if (!first && ci + 2 < NCH) load_state(Sa, c0 + 2 * C2);
+            process(Sb, c0 + C2);
+          }
+          // this thread's stores precede these loads of the same addresses
+          if (!last) load_state(Sa, cbeg);
+        } else {
 #pragma unroll 1
         for (int c0 = cbeg; c0 < cbeg + Cfg::EPI_COLS; c0 += CH) {
           uint32_t P[CH], L[CH], H[CH];
@@ -552,6 +624,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
               tmem_st16(t_hi + c0, H);
             }
           }
+        }
         }
         tmem_wait_st();
         tc_fence_before();

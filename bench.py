@@ -67,8 +67,13 @@ def make_inputs(n, k, m):
 
 
 class Clocks:
-    """Samples nvidia-smi during the timed region."""
+    """Samples the SM clock and the clock-event reasons of one GPU during the
+    timed region: NVML polled every few milliseconds (so short regions still
+    get samples), nvidia-smi at 200 ms when NVML is unavailable.  Read only."""
 
+    REASONS = {"hw_slowdown": "HwSlowdown", "hw_thermal_slowdown": "HwThermalSlowdown",
+               "sw_thermal_slowdown": "SwThermalSlowdown", "sw_power_cap": "SwPowerCap",
+               "hw_power_brake_slowdown": "HwPowerBrakeSlowdown"}
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -77,11 +82,60 @@ class Clocks:
         self.index = index
         self.proc = None
         self.lines = []
+        self.samples = []
+        self.mx = None
+        self.reasons = set()
+        self.stop_flag = threading.Event()
+        self.nvml = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            # the CUDA device's own GPU (NVML numbers GPUs ignoring CUDA_VISIBLE_DEVICES)
+            uuid = str(torch.cuda.get_device_properties(index).uuid)
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(
+                uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.mx = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.bits = {}
+            for name, suffix in self.REASONS.items():
+                v = getattr(pynvml, "nvmlClocksEventReason" + suffix,
+                            getattr(pynvml, "nvmlClocksThrottleReason" + suffix, None))
+                if v is not None:
+                    self.bits[name] = v
+        except Exception:
+            self.nvml = None
+        self.smi_id = str(index)
+        try:
+            import torch
+            u = str(torch.cuda.get_device_properties(index).uuid)
+            self.smi_id = u if u.startswith("GPU-") else "GPU-" + u
+        except Exception:
+            pass
+
+    def _poll(self):
+        nv = self.nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                              getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                r = get_reasons(self.handle) if get_reasons else 0
+                for name, bit in self.bits.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.005)
 
     def start(self):
+        if self.nvml is not None:
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                ["nvidia-smi", f"--id={self.smi_id}", f"--query-gpu={self.Q}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
@@ -94,6 +148,12 @@ class Clocks:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            self.stop_flag.set()
+            self.t.join(timeout=2)
+            sm = self.samples
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.mx,
+                    "reasons": sorted(self.reasons), "samples": len(sm), "source": "nvml"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -116,7 +176,7 @@ class Clocks:
                 if v.lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 def cpu_oracle_sample(A, B, n_hi, n_lo, budget_s=12.0, max_rows=1024):

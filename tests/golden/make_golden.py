@@ -84,8 +84,11 @@ def cases():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("OZAKI_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("OZAKI_REF"),
+                    help="checkout of the reference project (or set OZAKI_REF)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref or set OZAKI_REF to the reference checkout")
     sys.path.insert(0, os.path.join(HERE, "refshim"))
     sys.path.insert(0, args.ref)
     import importlib

@@ -130,8 +130,28 @@ __device__ __forceinline__ void bulk_load_g2s(void* dst, const void* src, uint32
       : "memory");
 }
 
+// Untiled bulk copy shared (this CTA) -> global, tracked by this thread's bulk
+// groups.  dst and src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_store_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+               ::"l"((uint64_t)dst), "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Every committed bulk store of this thread has read its shared-memory source.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Every committed bulk store of this thread is complete.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // Orders this thread's earlier generic-proxy shared-memory accesses before
-// its later async-proxy ones (a bulk copy into a buffer just read).
+// its later async-proxy ones (a bulk copy into a buffer just read, or out of
+// a buffer just written).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -425,6 +445,61 @@ __device__ __forceinline__ float ld_dsmem_f32(const float* p, uint32_t rank) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
   return v;
+}
+
+// Relaxed 64-bit store to this CTA's shared memory: one single-copy-atomic word.
+__device__ __forceinline__ void st_smem_relaxed_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.cluster.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(p)), "l"(v) : "memory");
+}
+
+// Relaxed 64-bit load from the shared memory of CTA `rank` of this cluster (this
+// CTA included) at the offset of the local object `p`.
+__device__ __forceinline__ uint64_t ld_dsmem_relaxed_u64(const uint64_t* p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
+  uint64_t v;
+  asm volatile("ld.relaxed.cluster.shared::cluster.b64 %0, [%1];" : "=l"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// Bounded wait for a tagged word of CTA `rank`: (tag << 32) | value, written
+// with st_smem_relaxed_u64.  Tag and value travel in one atomic word, so a
+// matching tag proves the value current without release/acquire ordering.
+// Returns the value; gives up like mbar_wait (returns false, sets *abort and
+// OZK_FLAG_TIMEOUT in *status) after budget_ns or once *abort is set.
+__device__ __forceinline__ bool tag_wait(const uint64_t* p, uint32_t rank, uint32_t tag,
+                                         uint32_t& val, volatile int* abort, int32_t* status,
+                                         uint64_t budget_ns) {
+  uint64_t w = ld_dsmem_relaxed_u64(p, rank);
+  if ((uint32_t)(w >> 32) == tag) {
+    val = (uint32_t)w;
+    return true;
+  }
+  val = 0;
+  if (*abort) return false;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    w = ld_dsmem_relaxed_u64(p, rank);
+    if ((uint32_t)(w >> 32) == tag) {
+      val = (uint32_t)w;
+      return true;
+    }
+    if ((i & 31) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > budget_ns) {
+        *abort = 1;
+        raise_flag(status, OZK_FLAG_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// Cluster barrier without memory ordering (arrive.relaxed): the data that
+// crosses it carries tags instead (tag_wait).
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::
+                   : "memory");
 }
 
 // Named barrier among `nthreads` threads (multiple of 32).

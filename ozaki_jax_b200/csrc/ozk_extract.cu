@@ -316,16 +316,26 @@ __global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
 
 // ---------------------------------------------------------------- rows, staged by bulk copies
 
-// Rows of 1024 < K <= 12288 FP64 values (even K, 16-byte aligned rows): a
-// persistent CTA of NT threads walks rows blockIdx.x, += gridDim.x.  A row
-// arrives in shared memory through bulk copies, is moved into registers (EPT
-// columns per thread, in groups of four adjacent columns) and split, and the
-// buffer is refilled with the CTA's next row at once, so its DRAM transfer
-// overlaps the slice passes of this one; several CTAs per SM keep several
-// rows in flight.  Each slice pass also takes the maximum of the new residual
-// for the next pass, so a pass is one block reduction plus one register sweep.
-// Slices are written as 8-byte (BF16) or 4-byte (int8) words, all columns up
-// to k_pad included.
+// Rows of 1024 < K <= 65536 FP64 values (even K, 16-byte aligned rows): a
+// persistent CTA of NT threads (or a cluster of CL CTAs, each owning NT*EPT
+// columns) walks rows blockIdx.x / CL, += gridDim.x / CL.  A row arrives in
+// shared memory through bulk copies, is moved into registers (EPT columns per
+// thread, in groups of four adjacent columns) and split, and the buffer is
+// refilled with the CTA's next row at once, so its DRAM transfer overlaps the
+// slice passes of this one; several CTAs per SM keep several rows in flight.
+//
+// A slice pass is one barrier: each warp posts its partial line maxima, and
+// after the barrier every warp reduces all partials of the line and derives
+// the slice parameters itself, then sweeps its registers, taking the next
+// pass's maxima on the way.  In a cluster the barrier is the cluster's, with
+// relaxed arrival (a release would wait for this thread's code stores still
+// in flight), and each partial is one 64-bit word (pass << 32) | FP32 bits:
+// a reader in any CTA of the cluster takes it once the tag matches.  Two
+// parity slots suffice, as a slot is rewritten only after the next barrier,
+// which no thread passes before its reads of the slot are done.  Slices are
+// written as 8-byte (BF16) or 4-byte (int8) words, all columns up to k_pad
+// included; clustered int8 lines stage them in shared memory (two buffers per
+// side), and one thread bulk-stores a pass's codes after the next barrier.
 //
 // int8 codes: with the slice exponent c of a line in [-127, 127 - rho] (and
 // the line finite), t = RN32(r + sigma) lies in [2^(rho+c-1), 2^(rho+c)), a
@@ -336,22 +346,46 @@ __global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
 // FP32 range) set *s8_fail instead, once per line.
 constexpr uint32_t kBulkChunk = 16384;  // bytes per bulk copy instruction
 
+template <bool S8, int CL>
+constexpr bool kStageCodes = S8 && CL > 1;
+
+// Dynamic shared memory of k_extract_rows_bulk: the row buffer, then (staged
+// codes) 2 buffers x 2 sides of NT*EPT int8 codes.
+template <int NT, int EPT, bool S8, int CL>
+inline size_t bulk_smem_bytes(int64_t K) {
+  return kStageCodes<S8, CL>
+             ? (size_t)NT * EPT * 8 + 4 * (size_t)NT * EPT
+             : (size_t)round_up((K < (int64_t)NT * EPT ? K : (int64_t)NT * EPT) * 8, 128);
+}
+
+// max(m, |a|, |b|) as one three-input maximum; like fmaxf, a NaN operand is
+// ignored in favour of the others.
+__device__ __forceinline__ float max3_abs(float m, float a, float b) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(m), "f"(fabsf(a)), "f"(fabsf(b)));
+  return d;
+}
+
 template <int NT, int EPT, int MINB, bool S8, int CL>
 __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
     const double* __restrict__ X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
     int n_lo, void* __restrict__ slices_v, int64_t k_pad, int32_t* __restrict__ exps,
     int32_t* status, int32_t* s8_fail, const int32_t* gate, uint64_t budget_ns) {
   static_assert(EPT % 4 == 0, "EPT must be a multiple of 4");
-  static_assert(NT / 32 <= 32, "one warp reduces the warp partials");
   constexpr int NG = EPT / 4;
   constexpr int NW = NT / 32;
+  constexpr int NP = NW * CL;  // partial maxima of a line: one per warp of the cluster
+  static_assert((NP & (NP - 1)) == 0 && NP <= 64, "NP: a power of two, at most 64");
+  constexpr int NPL = NP < 32 ? NP : 32;  // lanes holding partials
   constexpr int ESZ = S8 ? 1 : 2;  // bytes per slice element
+  constexpr bool STAGE = kStageCodes<S8, CL>;
+  constexpr uint32_t kCodeBytes = (uint32_t)NT * EPT;  // int8 codes of one slice of a CTA's columns
   if (gate && *(volatile const int32_t*)gate == 0) return;  // uniform over the grid
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ uint64_t s_bar;
-  __shared__ float s_part[2][2][NW];    // [parity][hi, lo][warp]
-  __shared__ float s_cta[2][3];         // [parity][hi max, lo max, line flags] for the cluster
-  __shared__ __align__(16) float s_prm[2][8];  // [parity][sig, inv, zero, c (hi); same (lo)]
+  __shared__ float s_part[2][2][NW];  // CL == 1: [parity][hi max, lo max][warp]
+  // CL > 1: [parity][hi, lo][warp], (pass << 32) | FP32 bits (lo: bit 31 = line flags)
+  __shared__ uint64_t s_tag[2][2][CL > 1 ? NW : 1];
   __shared__ int s_abort;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t crank = CL > 1 ? cluster_ctarank() : 0;
@@ -363,6 +397,10 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
   const int npass = n_hi > n_lo ? n_hi : n_lo;
   const int64_t slice_stride = rows * k_pad;
   const double* xb = reinterpret_cast<const double*>(smem_raw);
+  uint8_t* const s_code = smem_raw + (size_t)NT * EPT * 8;  // STAGE: [buffer][side][kCodeBytes]
+  // STAGE: code bytes of a slice this CTA writes, columns [kbase, min(k_pad, kbase + NT*EPT))
+  const uint32_t code_bytes =
+      (uint32_t)(k_pad - kbase <= 0 ? 0 : (k_pad - kbase < (int64_t)kCodeBytes ? k_pad - kbase : kCodeBytes));
   // groups of this thread that lie inside [0, k_pad): q < nq
   int nq = 0;
   {
@@ -376,12 +414,33 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
     s_abort = 0;
     fence_mbar_init();
   }
-  __syncthreads();
+  if constexpr (CL > 1)
+    if (tid < 4 * NW) (&s_tag[0][0][0])[tid] = ~0ull;  // no pass carries tag 0xffffffff
+  // the tagged slots are initialised before any peer reads them
+  if constexpr (CL > 1) cluster_sync();
+  else __syncthreads();
   auto issue = [&](int64_t row) {
     const uint8_t* src = reinterpret_cast<const uint8_t*>(X + row * ldx + kbase);
     mbar_arrive_expect_tx(&s_bar, own_bytes);
     for (uint32_t off = 0; off < own_bytes; off += kBulkChunk)
       bulk_load_g2s(smem_raw + off, src + off, min(kBulkChunk, own_bytes - off), &s_bar);
+  };
+  // STAGE: the codes of the last pass wait in s_code[pend_buf] for thread 0
+  // to store them after the next barrier.
+  bool pend = false;
+  int64_t pend_row = 0;
+  int pend_hi = -1, pend_lo = -1;
+  uint32_t pend_buf = 0;
+  auto flush = [&]() {
+    if (code_bytes) {
+      uint8_t* dst = static_cast<uint8_t*>(slices_v) + pend_row * k_pad + kbase;
+      if (pend_hi >= 0)
+        bulk_store_s2g(dst + pend_hi * slice_stride, s_code + (2 * pend_buf) * kCodeBytes, code_bytes);
+      if (pend_lo >= 0)
+        bulk_store_s2g(dst + pend_lo * slice_stride, s_code + (2 * pend_buf + 1) * kCodeBytes,
+                       code_bytes);
+    }
+    bulk_commit();
   };
   // A cluster's CTAs go through every row together.  If a wait runs out of
   // time the CTA keeps stepping with its peers (so no cluster barrier is left
@@ -395,13 +454,15 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
     ++issued;
   }
   uint32_t it = 0, par = 0;
+  uint32_t gpass = 0;  // passes so far over all rows: the mailbox tag
   for (int64_t row = row0; row < rows; row += rstride, ++it) {
     bool got = true;
     if (live && own_bytes)
       got = mbar_wait(&s_bar, it & 1, (volatile int*)&s_abort, status, budget_ns);
     if (__syncthreads_or(!got)) live = false;
     else if (live && own_bytes) ++landed;
-    float rh[EPT], rl[EPT];
+    // residuals in pairs of adjacent columns, for the packed FP32 arithmetic
+    float2 rh[EPT / 2], rl[EPT / 2];
     float mh = 0.0f, ml = 0.0f;
     bool odd = false;  // a non-finite split value: the input is non-finite or beyond FP32
 #pragma unroll
@@ -418,13 +479,14 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
           if (k + h < kown) x[h] = xb[k + h];
       }
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        float& hi = rh[4 * q + h];
-        float& lo = rl[4 * q + h];
-        split_f64(x[h], hi, lo);
-        odd |= !(fabsf(hi) <= 3.402823466e38f);
-        mh = fmaxf(mh, fabsf(hi));
-        ml = fmaxf(ml, fabsf(lo));
+      for (int j = 0; j < 2; ++j) {
+        float2& hi = rh[2 * q + j];
+        float2& lo = rl[2 * q + j];
+        split_f64(x[2 * j], hi.x, lo.x);
+        split_f64(x[2 * j + 1], hi.y, lo.y);
+        odd |= !(fmaxf(fabsf(hi.x), fabsf(hi.y)) <= 3.402823466e38f);
+        mh = max3_abs(mh, hi.x, hi.y);
+        ml = max3_abs(ml, lo.x, lo.y);
       }
     }
     int32_t flags = 0;
@@ -434,7 +496,8 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
           const int64_t k = 4 * ((int64_t)q * NT + tid) + h;
-          if (k < kown) flags |= check_value(xb[k], rh[4 * q + h]);
+          const float2 hp = rh[2 * q + (h >> 1)];
+          if (k < kown) flags |= check_value(xb[k], (h & 1) ? hp.y : hp.x);
         }
       raise_flag(status, flags);
     }
@@ -449,68 +512,81 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         ++issued;
       }
     }
-    for (int t = 0; t < npass; ++t, par ^= 1) {
+    for (int t = 0; t < npass; ++t, par ^= 1, ++gpass) {
       const bool do_hi = t < n_hi, do_lo = t < n_lo;
-      // Line maxima: warp shuffles, then warp 0 over the warps (and the
-      // cluster), which also derives the slice parameters for everyone.
+      // Partial line maxima of each warp (and, in the first pass, the line's
+      // input flags), one barrier, then the line maxima in every warp.
 #pragma unroll
       for (int o = 16; o; o >>= 1) {
         mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
         ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, o));
       }
-      if (lane == 0) {
-        s_part[par][0][warp] = mh;
-        s_part[par][1][warp] = ml;
-      }
-      __syncthreads();
-      if (warp == 0) {
-        mh = lane < NW ? s_part[par][0][lane] : 0.0f;
-        ml = lane < NW ? s_part[par][1][lane] : 0.0f;
+      bool bad = t == 0 && line_bad;
+      float gh = 0.0f, gl = 0.0f;
+      if constexpr (CL == 1) {
+        if (lane == 0) {
+          s_part[par][0][warp] = mh;
+          s_part[par][1][warp] = ml;
+        }
+        __syncthreads();
+        if (lane < NW) {
+          gh = s_part[par][0][lane];
+          gl = s_part[par][1][lane];
+        }
+      } else {
+        if (lane == 0) {
+          const uint64_t tag = (uint64_t)gpass << 32;
+          st_smem_relaxed_u64(&s_tag[par][0][warp], tag | __float_as_uint(mh));
+          st_smem_relaxed_u64(&s_tag[par][1][warp],
+                              tag | __float_as_uint(ml) | (bad ? 0x80000000u : 0u));
+        }
+        if constexpr (STAGE) {
+          fence_proxy_async_smem();            // this thread's staged codes, for the bulk store
+          if (tid == 0) bulk_wait_read_all();  // the buffer this pass writes is no longer read
+        }
+        cluster_sync_relaxed();
+        if constexpr (STAGE) {
+          if (tid == 0 && pend) flush();
+          pend = false;
+        }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) {
-          mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
-          ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, o));
-        }
-      }
-      int lbad = line_bad;
-      if constexpr (CL > 1) {
-        // line maxima (and, in the first pass, the line's input flags) over
-        // the cluster through distributed shared memory
-        if (tid == 0) {
-          s_cta[par][0] = mh;
-          s_cta[par][1] = ml;
-          s_cta[par][2] = (float)line_bad;
-        }
-        cluster_sync();
-        if (warp == 0) {
-          for (uint32_t r = 0; r < (uint32_t)CL; ++r) {
-            mh = fmaxf(mh, ld_dsmem_f32(&s_cta[par][0], r));
-            ml = fmaxf(ml, ld_dsmem_f32(&s_cta[par][1], r));
-            if (t == 0 && ld_dsmem_f32(&s_cta[par][2], r) != 0.0f) lbad = 1;
+        for (int e0 = 0; e0 < NP; e0 += 32) {
+          const int e = e0 + lane;
+          if (e < NP) {
+            uint32_t vh, vl;
+            tag_wait(&s_tag[par][0][e % NW], (uint32_t)(e / NW), gpass, vh,
+                     (volatile int*)&s_abort, status, budget_ns);
+            tag_wait(&s_tag[par][1][e % NW], (uint32_t)(e / NW), gpass, vl,
+                     (volatile int*)&s_abort, status, budget_ns);
+            gh = fmaxf(gh, __uint_as_float(vh));
+            gl = fmaxf(gl, __uint_as_float(vl & 0x7fffffffu));
+            bad = bad || (vl >> 31);
           }
         }
+        bad = __any_sync(0xffffffffu, bad);
       }
-      if (warp == 0 && lane == 0) {
-        float sh = 0.f, ih = 0.f, sl = 0.f, il = 0.f;
-        int zh = 1, zl = 1, ch = 0, cl = 0;
-        if (do_hi) slice_params(mh, rho, sh, ih, zh, ch);
-        if (do_lo) slice_params(ml, rho, sl, il, zl, cl);
+#pragma unroll
+      for (int o = NPL / 2; o; o >>= 1) {
+        gh = fmaxf(gh, __shfl_xor_sync(0xffffffffu, gh, o));
+        gl = fmaxf(gl, __shfl_xor_sync(0xffffffffu, gl, o));
+      }
+      if constexpr (NPL < 32) {  // lanes past NPL reduced zeros: take lane 0's
+        gh = __shfl_sync(0xffffffffu, gh, 0);
+        gl = __shfl_sync(0xffffffffu, gl, 0);
+      }
+      float sh = 0.f, ih = 0.f, sl = 0.f, il = 0.f;
+      int zh = 1, zl = 1, ch = 0, cl = 0;
+      if (do_hi) slice_params(gh, rho, sh, ih, zh, ch);
+      if (do_lo) slice_params(gl, rho, sl, il, zl, cl);
+      if (tid == 0 && crank == 0) {
         if (S8) {
-          bool bad = t == 0 && lbad;
           if (do_hi && !zh && (ch < -127 || rho + ch > 127)) bad = true;
           if (do_lo && !zl && (cl < -127 || rho + cl > 127)) bad = true;
-          if (bad && crank == 0) *s8_fail = 1;
+          if (bad) *s8_fail = 1;
         }
-        if (crank == 0) {
-          if (do_hi) exps[(int64_t)t * rows + row] = ch;
-          if (do_lo) exps[(int64_t)(n_hi + t) * rows + row] = cl;
-        }
-        *reinterpret_cast<float4*>(&s_prm[par][0]) = make_float4(sh, ih, 0.f, 0.f);
-        *reinterpret_cast<float4*>(&s_prm[par][4]) = make_float4(sl, il, 0.f, 0.f);
+        if (do_hi) exps[(int64_t)t * rows + row] = ch;
+        if (do_lo) exps[(int64_t)(n_hi + t) * rows + row] = cl;
       }
-      __syncthreads();
-      const float4 ph = *reinterpret_cast<const float4*>(&s_prm[par][0]);
-      const float4 pl = *reinterpret_cast<const float4*>(&s_prm[par][4]);
       mh = 0.0f;
       ml = 0.0f;
       // A zero line has all residuals 0, so RN(r + sigma) - sigma is 0 there and
@@ -518,24 +594,36 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
 #pragma unroll
       for (int side = 0; side < 2; ++side) {
         if (side == 0 ? !do_hi : !do_lo) continue;
-        const float sg = side == 0 ? ph.x : pl.x, iv = side == 0 ? ph.y : pl.y;
+        const float sg = side == 0 ? sh : sl, iv = side == 0 ? ih : il;
         const uint32_t sg_bits = __float_as_uint(sg);
-        uint8_t* out = static_cast<uint8_t*>(slices_v) +
-                       ((int64_t)(side == 0 ? t : n_hi + t) * slice_stride + row * k_pad + kbase +
-                        4 * (int64_t)tid) * ESZ;
+        const float2 sg2 = make_float2(sg, sg), nsg2 = make_float2(-sg, -sg);
+        const float2 iv2 = make_float2(iv, iv);
+        uint8_t* out;
+        if constexpr (STAGE)
+          out = s_code + (2 * par + side) * kCodeBytes + 4 * tid;
+        else
+          out = static_cast<uint8_t*>(slices_v) +
+                ((int64_t)(side == 0 ? t : n_hi + t) * slice_stride + row * k_pad + kbase +
+                 4 * (int64_t)tid) * ESZ;
         float mnext = 0.0f;
 #pragma unroll
         for (int q = 0; q < NG; ++q) {
           uint32_t u[4];
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            float& r = side == 0 ? rh[4 * q + h] : rl[4 * q + h];
-            const float tt = __fadd_rn(r, sg);
-            const float v = __fsub_rn(tt, sg);
-            r = __fsub_rn(r, v);
-            mnext = fmaxf(mnext, fabsf(r));
-            if constexpr (S8) u[h] = __float_as_uint(tt) - sg_bits;  // the int8 code
-            else u[h] = __float_as_uint(__fmul_rn(v, iv));           // BF16 in the top half
+          for (int j = 0; j < 2; ++j) {
+            float2& r = side == 0 ? rh[2 * q + j] : rl[2 * q + j];
+            const float2 tt = __fadd2_rn(r, sg2);   // RN(r + sigma)
+            const float2 v = __fadd2_rn(tt, nsg2);  // the slice value, exact
+            r = __fadd2_rn(r, make_float2(-v.x, -v.y));  // exact
+            mnext = max3_abs(mnext, r.x, r.y);
+            if constexpr (S8) {  // the int8 codes
+              u[2 * j] = __float_as_uint(tt.x) - sg_bits;
+              u[2 * j + 1] = __float_as_uint(tt.y) - sg_bits;
+            } else {  // BF16 in the top halves
+              const float2 b = __fmul2_rn(v, iv2);
+              u[2 * j] = __float_as_uint(b.x);
+              u[2 * j + 1] = __float_as_uint(b.y);
+            }
           }
           if constexpr (!S8) {
             // columns K..k_pad-1 are zeros even where 2^-c is not finite
@@ -546,20 +634,35 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
                 if (k + h >= K) u[h] = 0;
             }
           }
-          if (q < nq) {
-            if constexpr (S8) {
-              const uint32_t w = __byte_perm(__byte_perm(u[0], u[1], 0x0040),
-                                             __byte_perm(u[2], u[3], 0x0040), 0x5410);
-              *reinterpret_cast<uint32_t*>(out + (int64_t)q * 4 * NT) = w;
-            } else {
-              *reinterpret_cast<uint2*>(out + (int64_t)q * 8 * NT) =
-                  make_uint2(__byte_perm(u[0], u[1], 0x7632), __byte_perm(u[2], u[3], 0x7632));
-            }
+          if constexpr (S8) {
+            const uint32_t w = __byte_perm(__byte_perm(u[0], u[1], 0x0040),
+                                           __byte_perm(u[2], u[3], 0x0040), 0x5410);
+            // staged: every group (the bulk store takes the first code_bytes)
+            if (STAGE || q < nq) *reinterpret_cast<uint32_t*>(out + (int64_t)q * 4 * NT) = w;
+          } else if (q < nq) {
+            *reinterpret_cast<uint2*>(out + (int64_t)q * 8 * NT) =
+                make_uint2(__byte_perm(u[0], u[1], 0x7632), __byte_perm(u[2], u[3], 0x7632));
           }
         }
         if (side == 0) mh = mnext;
         else ml = mnext;
       }
+      if constexpr (STAGE) {
+        pend = true;
+        pend_row = row;
+        pend_hi = do_hi ? t : -1;
+        pend_lo = do_lo ? n_hi + t : -1;
+        pend_buf = par;
+      }
+    }
+  }
+  if constexpr (STAGE) {
+    // the last pass's codes
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      if (pend) flush();
+      bulk_wait_all();
     }
   }
   // Every issued copy lands before the CTA's shared memory is released.
@@ -568,7 +671,7 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
       mbar_wait(&s_bar, j & 1, nullptr, status, budget_ns);
   }
   __syncthreads();
-  if constexpr (CL > 1) cluster_sync();  // peers may still read this CTA's s_cta
+  if constexpr (CL > 1) cluster_sync();  // no peer reads this CTA's tagged slots any more
 }
 
 // ---------------------------------------------------------------- transpose
@@ -942,7 +1045,7 @@ static int launch_rows_bulk(const double* X, int64_t ldx, int64_t rows, int64_t 
                             int n_hi, int n_lo, void* slices, int64_t k_pad, int32_t* exps,
                             int32_t* status, int32_t* s8_fail, const int32_t* gate, int dev,
                             cudaStream_t stream) {
-  constexpr size_t kMaxSmem = (size_t)EPT * NT * 8;
+  const size_t kMaxSmem = bulk_smem_bytes<NT, EPT, S8, CL>((int64_t)NT * EPT);
   auto kern = k_extract_rows_bulk<NT, EPT, MINB, S8, CL>;
   static int configured[64] = {0};
   if (!configured[dev]) {
@@ -953,14 +1056,12 @@ static int launch_rows_bulk(const double* X, int64_t ldx, int64_t rows, int64_t 
     configured[dev] = 1;
   }
   // CTA r of a cluster stages columns [r*NT*EPT, (r+1)*NT*EPT) of a row
-  const size_t smem = (size_t)round_up((K < (int64_t)NT * EPT ? K : (int64_t)NT * EPT) * 8, 128);
+  const size_t smem = bulk_smem_bytes<NT, EPT, S8, CL>(K);
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem) != cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
   int64_t clusters = (int64_t)device_sm_count(dev) * per_sm / CL;
-  if (clusters > rows) clusters = rows;
-  if (clusters < 1) clusters = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(clusters * CL));
   cfg.blockDim = dim3(NT);
@@ -973,6 +1074,21 @@ static int launch_rows_bulk(const double* X, int64_t ldx, int64_t rows, int64_t 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (CL > 1) {
+    // Only as many clusters as are resident at once: a GPC need not hold a
+    // whole number of them, and a second wave of clusters would double the
+    // time of the persistent row loop.
+    static int fit[64] = {0};
+    if (!fit[dev]) {
+      int n = 0;
+      fit[dev] = (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) ? n : -1;
+      cudaGetLastError();
+    }
+    if (fit[dev] > 0 && fit[dev] < clusters) clusters = fit[dev];
+  }
+  if (clusters > rows) clusters = rows;
+  if (clusters < 1) clusters = 1;
+  cfg.gridDim = dim3((unsigned)(clusters * CL));
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
                                      exps, status, s8_fail, gate, wait_budget_ns());
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows_bulk launch", e);
@@ -1009,8 +1125,12 @@ static int launch_rows_bulk_any(const double* X, int64_t ldx, int64_t rows, int6
   if (k_pad <= 12288)
     return launch_rows_bulk<512, 24, 1, S8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
                                             status, s8_fail, gate, dev, stream);
-  // Longer rows: a cluster of CTAs per row, 16384 columns each, line maxima
-  // exchanged through distributed shared memory.
+  // Longer rows: a cluster of CTAs per row, line maxima exchanged through
+  // distributed shared memory; 8192 columns per CTA (two CTAs per SM) up to
+  // 16384, 16384 columns per CTA beyond.
+  if (k_pad <= 16384)
+    return launch_rows_bulk<256, 32, 2, S8, 2>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
+                                               exps, status, s8_fail, gate, dev, stream);
   if (k_pad <= 32768)
     return launch_rows_bulk<512, 32, 1, S8, 2>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
                                                exps, status, s8_fail, gate, dev, stream);
@@ -1030,7 +1150,8 @@ int launch_extract_rows_s8(const double* X, int64_t ldx, int64_t rows, int64_t K
   cudaGetDevice(&dev);
   int rc = upload_log2_table(dev);
   if (rc) return rc;
-  if (bulk_rows_ok(X, ldx, K, k_pad))
+  // (the clustered variants bulk-store 16-byte aligned rows of codes)
+  if (bulk_rows_ok(X, ldx, K, k_pad) && ((uintptr_t)slices & 15) == 0)
     return launch_rows_bulk_any<true>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
                                       status, s8_fail, nullptr, dev, stream);
   // rho >= 19 means K > 4096, so 8192-column CTAs (and clusters for longer lines)

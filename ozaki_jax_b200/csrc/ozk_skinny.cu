@@ -13,8 +13,16 @@
 // kernel's, so results are bit-identical to it) runs once per tile.
 //
 // Warp 0: TMA producer.  Warp 1: TMEM allocation and the MMA issuer (one
-// thread, tcgen05.mma.cta_group::1.kind::i8, M = 128, N = 16, K = 32).
-// Warps 2-5: epilogue, one output row per thread.
+// thread, tcgen05.mma.cta_group::1.kind::i8, M = 128, K = 32).  Warps 2-5:
+// epilogue, one output row per thread.
+//
+// The pairs are taken in (A slice, X slice) order, and the pairs of one A
+// slice with consecutive X slices form a run: the X slices' 16-row tiles lie
+// back to back in shared memory and their accumulators side by side in TMEM,
+// so a run is ONE MMA of N = 16 * (run length).  For the preset (4, 1) that
+// is 5 MMAs per k-step instead of 24, and each A tile is read from shared
+// memory once per run rather than once per pair (at N = 16 the A operand's
+// shared-memory reads, not the tensor math, bound an MMA).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -37,9 +45,12 @@ constexpr int kSkXBytes = kSkCols * kS8KB;   // one slice's k-block of X: 2 KB
 constexpr int kSkThreads = 192;
 
 struct SkPairs {
-  uint8_t a[kSkMaxPairs];
-  uint8_t b[kSkMaxPairs];
+  uint8_t a[kSkMaxPairs];  // pairs sorted by (a, b); pair p accumulates in TMEM columns
+  uint8_t b[kSkMaxPairs];  // [16 p, 16 p + 16)
   int n;
+  uint8_t run_p0[kSkMaxPairs];   // first pair of each run
+  uint8_t run_len[kSkMaxPairs];  // pairs in the run (<= 16: N <= 256)
+  int n_runs;
 };
 
 struct SkArgs {
@@ -132,7 +143,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_s8(kSkRows, kSkCols);
+      constexpr uint32_t idesc0 = umma_idesc_s8(kSkRows, 0);
       uint32_t it = 0, tile_it = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x, ++tile_it) {
@@ -145,12 +156,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             break;
           }
           tc_fence_after();
-          for (int p = 0; p < pairs.n; ++p) {
-            const uint32_t a0 = smem_u32(a_tile(s, pairs.a[p]));
-            const uint32_t x0 = smem_u32(x_tile(s, pairs.b[p]));
+          for (int r = 0; r < pairs.n_runs; ++r) {
+            const int p0 = pairs.run_p0[r];
+            const uint32_t a0 = smem_u32(a_tile(s, pairs.a[p0]));
+            const uint32_t x0 = smem_u32(x_tile(s, pairs.b[p0]));
+            // N = 16 * len: the N field holds N / 8
+            const uint32_t idesc = idesc0 | ((uint32_t)(2 * pairs.run_len[r]) << 17);
 #pragma unroll
             for (int kk = 0; kk < kS8KB / 32; ++kk)
-              umma_s8(tmem + p * kSkCols, umma_desc_sw128(a0 + kk * 32),
+              umma_s8(tmem + p0 * kSkCols, umma_desc_sw128(a0 + kk * 32),
                       umma_desc_sw128(x0 + kk * 32), idesc, (kb | kk) != 0);
           }
           umma_commit(&empty[s]);
@@ -266,13 +280,34 @@ int launch_skinny_s8(const int8_t* SA, const int32_t* eA, const int8_t* SX, cons
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k_skinny_s8)", e);
     configured[dev] = 1;
   }
+  // Pairs sorted by (a, b) (the fixed-point sum does not depend on the
+  // order), then cut into runs of consecutive b under one a.
   SkPairs pl;
   memset(&pl, 0, sizeof(pl));
+  int order[kSkMaxPairs];
+  for (int p = 0; p < n_pairs; ++p) order[p] = p;
+  for (int i = 1; i < n_pairs; ++i)
+    for (int j = i; j > 0; --j) {
+      const int u = order[j - 1], v = order[j];
+      if (pair_a[u] < pair_a[v] || (pair_a[u] == pair_a[v] && pair_b[u] <= pair_b[v])) break;
+      order[j - 1] = v;
+      order[j] = u;
+    }
   for (int p = 0; p < n_pairs; ++p) {
-    pl.a[p] = pair_a[p];
-    pl.b[p] = pair_b[p];
+    pl.a[p] = pair_a[order[p]];
+    pl.b[p] = pair_b[order[p]];
   }
   pl.n = n_pairs;
+  for (int p = 0; p < n_pairs; ++p) {
+    const int r = pl.n_runs - 1;
+    if (p > 0 && pl.a[p] == pl.a[p - 1] && pl.b[p] == pl.b[p - 1] + 1 && pl.run_len[r] < 16) {
+      ++pl.run_len[r];
+    } else {
+      pl.run_p0[pl.n_runs] = (uint8_t)p;
+      pl.run_len[pl.n_runs] = 1;
+      ++pl.n_runs;
+    }
+  }
   SkArgs ga;
   memset(&ga, 0, sizeof(ga));
   ga.eA = eA;

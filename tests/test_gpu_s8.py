@@ -60,7 +60,7 @@ def bf16_values(bits):
 
 @pytest.mark.parametrize("axis", [1, 0])
 @pytest.mark.parametrize("K,n_hi,n_lo", [(4097, 4, 1), (8192, 3, 1), (5000, 5, 4), (12000, 4, 1),
-                                         (20000, 4, 1)])
+                                         (20000, 4, 1), (32768, 4, 1), (40000, 3, 2)])
 def test_codes_are_the_bf16_slices(axis, K, n_hi, n_lo):
     rng = np.random.RandomState(K + axis)
     lines = 300

@@ -334,8 +334,9 @@ __global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
 // parity slots suffice, as a slot is rewritten only after the next barrier,
 // which no thread passes before its reads of the slot are done.  Slices are
 // written as 8-byte (BF16) or 4-byte (int8) words, all columns up to k_pad
-// included; clustered int8 lines stage them in shared memory (two buffers per
-// side), and one thread bulk-stores a pass's codes after the next barrier.
+// included; int8 codes are staged in shared memory (two buffers per side), and
+// one thread bulk-stores a pass's codes after the next barrier, which takes
+// the address arithmetic and most store instructions off the sweeps.
 //
 // int8 codes: with the slice exponent c of a line in [-127, 127 - rho] (and
 // the line finite), t = RN32(r + sigma) lies in [2^(rho+c-1), 2^(rho+c)), a
@@ -347,7 +348,7 @@ __global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
 constexpr uint32_t kBulkChunk = 16384;  // bytes per bulk copy instruction
 
 template <bool S8, int CL>
-constexpr bool kStageCodes = S8 && CL > 1;
+constexpr bool kStageCodes = S8;
 
 // Dynamic shared memory of k_extract_rows_bulk: the row buffer, then (staged
 // codes) 2 buffers x 2 sides of NT*EPT int8 codes.
@@ -366,17 +367,21 @@ __device__ __forceinline__ float max3_abs(float m, float a, float b) {
   return d;
 }
 
-template <int NT, int EPT, int MINB, bool S8, int CL>
+// PRESET = 16 n_hi + n_lo fixes the slice counts at compile time (the pass
+// loop unrolls, the lo residuals die after their last pass); 0 takes them
+// from the arguments.
+template <int NT, int EPT, int MINB, bool S8, int CL, int PRESET>
 __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
-    const double* __restrict__ X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi,
-    int n_lo, void* __restrict__ slices_v, int64_t k_pad, int32_t* __restrict__ exps,
+    const double* __restrict__ X, int64_t ldx, int64_t rows, int64_t K, int rho, int n_hi_arg,
+    int n_lo_arg, void* __restrict__ slices_v, int64_t k_pad, int32_t* __restrict__ exps,
     int32_t* status, int32_t* s8_fail, const int32_t* gate, uint64_t budget_ns) {
+  const int n_hi = PRESET ? PRESET / 16 : n_hi_arg;
+  const int n_lo = PRESET ? PRESET % 16 : n_lo_arg;
   static_assert(EPT % 4 == 0, "EPT must be a multiple of 4");
   constexpr int NG = EPT / 4;
   constexpr int NW = NT / 32;
   constexpr int NP = NW * CL;  // partial maxima of a line: one per warp of the cluster
-  static_assert((NP & (NP - 1)) == 0 && NP <= 64, "NP: a power of two, at most 64");
-  constexpr int NPL = NP < 32 ? NP : 32;  // lanes holding partials
+  static_assert(NP <= 64, "at most two partials per lane");
   constexpr int ESZ = S8 ? 1 : 2;  // bytes per slice element
   constexpr bool STAGE = kStageCodes<S8, CL>;
   constexpr uint32_t kCodeBytes = (uint32_t)NT * EPT;  // int8 codes of one slice of a CTA's columns
@@ -512,43 +517,45 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         ++issued;
       }
     }
-    for (int t = 0; t < npass; ++t, par ^= 1, ++gpass) {
+#pragma unroll
+    for (int t = 0; t < (PRESET ? (PRESET / 16 > PRESET % 16 ? PRESET / 16 : PRESET % 16) : npass);
+         ++t, par ^= 1, ++gpass) {
       const bool do_hi = t < n_hi, do_lo = t < n_lo;
       // Partial line maxima of each warp (and, in the first pass, the line's
-      // input flags), one barrier, then the line maxima in every warp.
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
-        ml = fmaxf(ml, __shfl_xor_sync(0xffffffffu, ml, o));
-      }
+      // input flags), one barrier, then the line maxima in every warp.  The
+      // maxima are >= 0 and never NaN (max3_abs skips NaN operands), so their
+      // bit patterns order as unsigned integers: one redux per reduction.
+      mh = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mh)));
+      ml = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ml)));
       bool bad = t == 0 && line_bad;
       float gh = 0.0f, gl = 0.0f;
-      if constexpr (CL == 1) {
-        if (lane == 0) {
+      if (lane == 0) {
+        if constexpr (CL == 1) {
           s_part[par][0][warp] = mh;
           s_part[par][1][warp] = ml;
-        }
-        __syncthreads();
-        if (lane < NW) {
-          gh = s_part[par][0][lane];
-          gl = s_part[par][1][lane];
-        }
-      } else {
-        if (lane == 0) {
+        } else {
           const uint64_t tag = (uint64_t)gpass << 32;
           st_smem_relaxed_u64(&s_tag[par][0][warp], tag | __float_as_uint(mh));
           st_smem_relaxed_u64(&s_tag[par][1][warp],
                               tag | __float_as_uint(ml) | (bad ? 0x80000000u : 0u));
         }
-        if constexpr (STAGE) {
-          fence_proxy_async_smem();            // this thread's staged codes, for the bulk store
-          if (tid == 0) bulk_wait_read_all();  // the buffer this pass writes is no longer read
+      }
+      if constexpr (STAGE) {
+        fence_proxy_async_smem();            // this thread's staged codes, for the bulk store
+        if (tid == 0) bulk_wait_read_all();  // the buffer this pass writes is no longer read
+      }
+      if constexpr (CL == 1) __syncthreads();
+      else cluster_sync_relaxed();
+      if constexpr (STAGE) {
+        if (tid == 0 && pend) flush();
+        pend = false;
+      }
+      if constexpr (CL == 1) {
+        if (lane < NW) {
+          gh = s_part[par][0][lane];
+          gl = s_part[par][1][lane];
         }
-        cluster_sync_relaxed();
-        if constexpr (STAGE) {
-          if (tid == 0 && pend) flush();
-          pend = false;
-        }
+      } else {
 #pragma unroll
         for (int e0 = 0; e0 < NP; e0 += 32) {
           const int e = e0 + lane;
@@ -565,15 +572,8 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         }
         bad = __any_sync(0xffffffffu, bad);
       }
-#pragma unroll
-      for (int o = NPL / 2; o; o >>= 1) {
-        gh = fmaxf(gh, __shfl_xor_sync(0xffffffffu, gh, o));
-        gl = fmaxf(gl, __shfl_xor_sync(0xffffffffu, gl, o));
-      }
-      if constexpr (NPL < 32) {  // lanes past NPL reduced zeros: take lane 0's
-        gh = __shfl_sync(0xffffffffu, gh, 0);
-        gl = __shfl_sync(0xffffffffu, gl, 0);
-      }
+      gh = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(gh)));
+      gl = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(gl)));
       float sh = 0.f, ih = 0.f, sl = 0.f, il = 0.f;
       int zh = 1, zl = 1, ch = 0, cl = 0;
       if (do_hi) slice_params(gh, rho, sh, ih, zh, ch);
@@ -1040,13 +1040,13 @@ static int launch_rows_reg(const double* X, int64_t ldx, int64_t rows, int64_t K
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows_reg launch", e);
 }
 
-template <int NT, int EPT, int MINB, bool S8, int CL = 1>
-static int launch_rows_bulk(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
-                            int n_hi, int n_lo, void* slices, int64_t k_pad, int32_t* exps,
-                            int32_t* status, int32_t* s8_fail, const int32_t* gate, int dev,
-                            cudaStream_t stream) {
+template <int NT, int EPT, int MINB, bool S8, int CL = 1, int PRESET = 0>
+static int launch_rows_bulk_p(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                              int n_hi, int n_lo, void* slices, int64_t k_pad, int32_t* exps,
+                              int32_t* status, int32_t* s8_fail, const int32_t* gate, int dev,
+                              cudaStream_t stream) {
   const size_t kMaxSmem = bulk_smem_bytes<NT, EPT, S8, CL>((int64_t)NT * EPT);
-  auto kern = k_extract_rows_bulk<NT, EPT, MINB, S8, CL>;
+  auto kern = k_extract_rows_bulk<NT, EPT, MINB, S8, CL, PRESET>;
   static int configured[64] = {0};
   if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1094,7 +1094,31 @@ static int launch_rows_bulk(const double* X, int64_t ldx, int64_t rows, int64_t 
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_extract_rows_bulk launch", e);
 }
 
-// The bulk-staged kernel serves rows of 1024 < K, k_pad <= 12288 with even K
+// The presets 'high' (4, 1) and 'medium' (3, 1) get kernels with the slice
+// counts fixed at compile time; other counts take them at run time.
+template <int NT, int EPT, int MINB, bool S8, int CL = 1>
+static int launch_rows_bulk(const double* X, int64_t ldx, int64_t rows, int64_t K, int rho,
+                            int n_hi, int n_lo, void* slices, int64_t k_pad, int32_t* exps,
+                            int32_t* status, int32_t* s8_fail, const int32_t* gate, int dev,
+                            cudaStream_t stream) {
+  // (not for clustered BF16 lines, the gated recomputation: there the
+  // unrolled passes would spill)
+  if constexpr (S8 || CL == 1) {
+    if (n_hi == 4 && n_lo == 1)
+      return launch_rows_bulk_p<NT, EPT, MINB, S8, CL, 0x41>(X, ldx, rows, K, rho, n_hi, n_lo,
+                                                             slices, k_pad, exps, status, s8_fail,
+                                                             gate, dev, stream);
+    if (n_hi == 3 && n_lo == 1)
+      return launch_rows_bulk_p<NT, EPT, MINB, S8, CL, 0x31>(X, ldx, rows, K, rho, n_hi, n_lo,
+                                                             slices, k_pad, exps, status, s8_fail,
+                                                             gate, dev, stream);
+  }
+  return launch_rows_bulk_p<NT, EPT, MINB, S8, CL, 0>(X, ldx, rows, K, rho, n_hi, n_lo, slices,
+                                                      k_pad, exps, status, s8_fail, gate, dev,
+                                                      stream);
+}
+
+// The bulk-staged kernel serves rows of 1024 < K, k_pad <= 65536 with even K
 // and ldx and a 16-byte aligned base (OZK_EXTRACT_BULK=0 turns it off).
 static bool bulk_rows_ok(const double* X, int64_t ldx, int64_t K, int64_t k_pad) {
   static int on = -1;
@@ -1150,7 +1174,7 @@ int launch_extract_rows_s8(const double* X, int64_t ldx, int64_t rows, int64_t K
   cudaGetDevice(&dev);
   int rc = upload_log2_table(dev);
   if (rc) return rc;
-  // (the clustered variants bulk-store 16-byte aligned rows of codes)
+  // (bulk stores of the codes: 16-byte aligned rows)
   if (bulk_rows_ok(X, ldx, K, k_pad) && ((uintptr_t)slices & 15) == 0)
     return launch_rows_bulk_any<true>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
                                       status, s8_fail, nullptr, dev, stream);

@@ -1149,16 +1149,16 @@ static int launch_rows_bulk_any(const double* X, int64_t ldx, int64_t rows, int6
   if (k_pad <= 12288)
     return launch_rows_bulk<512, 24, 1, S8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
                                             status, s8_fail, gate, dev, stream);
-  // Longer rows: a cluster of CTAs per row, line maxima exchanged through
-  // distributed shared memory; 8192 columns per CTA (two CTAs per SM) up to
-  // 16384, 16384 columns per CTA beyond.
+  // Longer rows: a cluster of CTAs per row, 8192 columns each (two CTAs of
+  // different rows per SM), line maxima exchanged through distributed shared
+  // memory.
   if (k_pad <= 16384)
     return launch_rows_bulk<256, 32, 2, S8, 2>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
                                                exps, status, s8_fail, gate, dev, stream);
   if (k_pad <= 32768)
-    return launch_rows_bulk<512, 32, 1, S8, 2>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
+    return launch_rows_bulk<256, 32, 2, S8, 4>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
                                                exps, status, s8_fail, gate, dev, stream);
-  return launch_rows_bulk<512, 32, 1, S8, 4>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
+  return launch_rows_bulk<256, 32, 2, S8, 8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
                                              exps, status, s8_fail, gate, dev, stream);
 }
 

@@ -198,6 +198,13 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   return pol;
 }
 
+// 64-bit load served by L2, not L1: for data other SMs wrote with atomics.
+__device__ __forceinline__ long long ld_cg_s64(const long long* p) {
+  long long v;
+  asm volatile("ld.global.cg.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ long long ld_l2_hint(const long long* p, uint64_t pol) {
   long long v;
   asm volatile("ld.global.L1::no_allocate.L2::cache_hint.b64 %0, [%1], %2;"

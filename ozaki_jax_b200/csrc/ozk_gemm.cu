@@ -78,6 +78,17 @@ struct GemmArgs {
   unsigned long long* pace;
   int pace_slack;
   uint64_t pace_budget_ns;
+  // Work split (int8 wide tiles): tiles below dp_tiles go round-robin, whole;
+  // each of the r remaining tiles is cut into sk_chunks equal pair ranges, and
+  // unit u < r * sk_chunks takes chunk u / r of tile dp_tiles + u % r, so the
+  // units on one chunk run the same pairs of neighbouring tiles at once (their
+  // panels are shared in L2, as in the whole-tile waves).  A unit holding part
+  // of a tile's pairs adds its exact int64 partial sums into sk_sum and counts
+  // itself in sk_count; the last one to arrive writes C.  dp_tiles ==
+  // num_tiles: no split.
+  int dp_tiles, sk_chunks;
+  long long* sk_sum;       // [tile - dp_tiles][rank][column][row in CTA]
+  unsigned int* sk_count;  // [tile - dp_tiles][rank]
 };
 
 // PAIR = false: one CTA per output tile of 128 x BN.
@@ -129,6 +140,35 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& tm, i
   tn = r / gsz;
 }
 
+// The work items of a unit: its round-robin whole tiles (ndp), then at most
+// one chunk of a split tile (nsk).
+struct ItemRange {
+  int ndp, nsk;
+};
+
+__device__ __forceinline__ ItemRange item_range(const GemmArgs& g, int unit, int n_units) {
+  ItemRange r;
+  r.ndp = g.dp_tiles > unit ? (g.dp_tiles - unit + n_units - 1) / n_units : 0;
+  r.nsk = unit < (g.num_tiles - g.dp_tiles) * g.sk_chunks ? 1 : 0;
+  return r;
+}
+
+// Item i: tile t and its pairs [p0, p1).
+__device__ __forceinline__ void item_at(const GemmArgs& g, const ItemRange& r, int unit,
+                                        int n_units, int np, int i, int& t, int& p0, int& p1) {
+  if (i < r.ndp) {
+    t = unit + i * n_units;
+    p0 = 0;
+    p1 = np;
+    return;
+  }
+  const int rem = g.num_tiles - g.dp_tiles;
+  const int chunk = unit / rem;
+  t = g.dp_tiles + unit % rem;
+  p0 = chunk * np / g.sk_chunks;
+  p1 = (chunk + 1) * np / g.sk_chunks;
+}
+
 // FP64 value of P * 2^e for the FP32 product bits u (exact), built with
 // integer operations only: the FP32 exponent field moves to the FP64 one with
 // e added, the mantissa shifts by 29.  Falls back to FP64 multiplies when the
@@ -174,6 +214,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
   uint32_t* s_tmem = (uint32_t*)(mma_done + 1);
   volatile int* s_abort = (volatile int*)(s_tmem + 1);
 
+  __shared__ int s_sk_last;  // epilogue: this CTA completes a split tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0;  // 0 = MMA-issuing CTA
   const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
@@ -213,12 +254,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
       long long w_empty = 0;
       bool pacer = g.pace != nullptr && (!PAIR || rank == 0);
       long long walk = 0;  // pairs this unit has issued
-      for (int t = unit; ok && t < g.num_tiles; t += n_units) {
-        int tm, tn;
+      const ItemRange ir = item_range(g, unit, n_units);
+      for (int i = 0; ok && i < ir.ndp + ir.nsk; ++i) {
+        int t, p0, p1, tm, tn;
+        item_at(g, ir, unit, n_units, npairs, i, t, p0, p1);
         tile_coords(g, t, tm, tn);
         const int arow = tm * Cfg::TILE_M + (int)rank * kBM;
         const int brow = tn * BN + (int)rank * Cfg::CTA_N;
-        for (int p = 0; ok && p < npairs; ++p) {
+        for (int p = p0; ok && p < p1; ++p) {
           const int a = pairs.a[p], b = pairs.b[p];
           if (pacer && walk >= g.pace_slack) {
             const unsigned long long need =
@@ -244,7 +287,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
                 pk -= g.num_kb;
                 ++pp;
               }
-              if (pp < npairs && pk < g.num_kb) {
+              if (pp < p1 && pk < g.num_kb) {
                 tma_prefetch_3d(&mapA, pk * KBE, arow, pairs.a[pp]);
                 tma_prefetch_3d(&mapB, pk * KBE, brow, pairs.b[pp]);
               }
@@ -275,7 +318,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
         // A unit with fewer tiles (or one that stopped) counts as done with
         // every pair the longest walk has, so no one waits for it.
         const long long longest =
-            (long long)((g.num_tiles + n_units - 1) / n_units) * npairs;
+            (long long)((g.dp_tiles + n_units - 1) / n_units) * npairs +
+            (g.dp_tiles < g.num_tiles ? (npairs + g.sk_chunks - 1) / g.sk_chunks : 0);
         if (longest > walk) atomicAdd(g.pace, (unsigned long long)(longest - walk));
       }
       if (g.stats) g.stats[8 * blockIdx.x + 2] = (unsigned long long)w_empty;
@@ -295,8 +339,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
       uint32_t it = 0, acc_it = 0;
       bool ok = true;
       long long w_acc = 0, w_full = 0, w_head = 0, t_start = clock64();
-      for (int t = unit; ok && t < g.num_tiles; t += n_units) {
-        for (int p = 0; ok && p < npairs; ++p) {
+      const ItemRange ir = item_range(g, unit, n_units);
+      for (int i = 0; ok && i < ir.ndp + ir.nsk; ++i) {
+        int t, p0, p1;
+        item_at(g, ir, unit, n_units, npairs, i, t, p0, p1);
+        for (int p = p0; ok && p < p1; ++p) {
           const uint32_t buf = acc_it & 1, aph = (acc_it >> 1) & 1;
           long long c0 = clock64();
           if (!mbar_wait(&acce[buf], aph ^ 1, s_abort, g.status, g.budget_ns)) {
@@ -368,11 +415,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
     const uint32_t acce_leader = PAIR ? mapa_u32(&acce[0], 0) : 0;
     uint32_t acc_it = 0;
     bool ok = true;
-    long long ep_wait = 0, ep_busy = 0, ep_pairs = 0;
+    // (32-bit cycle sums: a launch lasts far fewer than 2^32 cycles)
+    uint32_t ep_wait = 0, ep_busy = 0, ep_pairs = 0;
     long long Sa[16], Sb[16];  // running sums of two column chunks (int8 wide tiles)
-    for (int t = unit; ok && t < g.num_tiles; t += n_units) {
-      int tm, tn;
+    const ItemRange ir = item_range(g, unit, n_units);
+    for (int i = 0; ok && i < ir.ndp + ir.nsk; ++i) {
+      int t, p0, p1, tm, tn;
+      item_at(g, ir, unit, n_units, npairs, i, t, p0, p1);
       tile_coords(g, t, tm, tn);
+      // part of the tile's pairs: the sums go to the split slot, not to C
+      const bool partial = p0 > 0 || p1 < npairs;
+      auto sk_slot = [&]() {
+        return g.sk_sum + ((int64_t)(t - g.dp_tiles) * 2 + rank) * (BN * kBM) + q * 32 + lane;
+      };
       const int64_t col0 = (int64_t)tn * BN;
       named_bar(1, NE);
       for (int e = etid; e < g.nB * BN; e += NE) {
@@ -387,21 +442,21 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
       const int64_t row = (int64_t)tm * Cfg::TILE_M + rank * kBM + q * 32 + lane;
       const bool rvalid = row < g.N;
       const int eA0 = rvalid ? g.eA[row] : 0;
-      for (int p = 0; p < npairs; ++p) {
+      for (int p = p0; p < p1; ++p) {
         const uint32_t buf = acc_it & 1, aph = (acc_it >> 1) & 1;
         int got = 1;
-        const long long e0 = clock64();
+        const uint32_t e0 = (uint32_t)clock64();
         if (lane == 0) got = mbar_wait(&accf[buf], aph, s_abort, g.status, g.budget_ns);
         got = __shfl_sync(0xffffffffu, got, 0);
         if (!got) {
           ok = false;
           break;
         }
-        const long long e1 = clock64();
+        const uint32_t e1 = (uint32_t)clock64();
         tc_fence_after();
         const int a = pairs.a[p], b = pairs.b[p];
         const int ea = rvalid ? g.eA[(int64_t)a * g.N + row] : 0;
-        const bool first = (p == 0), last = (p == npairs - 1);
+        const bool first = (p == p0), last = (p == p1 - 1);
         const uint32_t t_acc = tmem + lane_base + buf * BN;
         const uint32_t t_lo = tmem + lane_base + 2 * BN;
         const uint32_t t_hi = tmem + lane_base + 3 * BN;
@@ -418,22 +473,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
             for (int j = 0; j < C2; ++j)
               S[j] = ld_l2_hint((const long long*)(gst + (int64_t)(c0 + j) * kBM), l2keep);
           };
-          auto process = [&](const long long (&S)[C2], int c0) {
-            uint32_t P[C2];
-            tmem_ld16(t_acc + c0, P);
-            tmem_wait_ld();
-            long long acc[C2];
-#pragma unroll
-            for (int j = 0; j < C2; ++j) {
-              const int db = b == 0 ? 0 : s_eB[b * BN + c0 + j];  // eb - eB0
-              acc[j] = fixed_term_s32((int32_t)P[j], ta + db) + (first ? 0ll : S[j]);
-            }
-            if (!last) {
-#pragma unroll
-              for (int j = 0; j < C2; ++j)
-                st_l2_hint((long long*)(gst + (int64_t)(c0 + j) * kBM), acc[j], l2keep);
-              return;
-            }
+          // the FP64 results of a chunk's sums, alpha / beta applied, into C
+          auto store_c = [&](const long long (&acc)[C2], int c0) {
             if (!rvalid) return;
             double V[C2];
 #pragma unroll
@@ -462,6 +503,34 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
                 }
               }
             }
+          };
+          auto process = [&](const long long (&S)[C2], int c0) {
+            uint32_t P[C2];
+            tmem_ld16(t_acc + c0, P);
+            tmem_wait_ld();
+            long long acc[C2];
+#pragma unroll
+            for (int j = 0; j < C2; ++j) {
+              const int db = b == 0 ? 0 : s_eB[b * BN + c0 + j];  // eb - eB0
+              acc[j] = fixed_term_s32((int32_t)P[j], ta + db) + (first ? 0ll : S[j]);
+            }
+            if (!last) {
+#pragma unroll
+              for (int j = 0; j < C2; ++j)
+                st_l2_hint((long long*)(gst + (int64_t)(c0 + j) * kBM), acc[j], l2keep);
+              return;
+            }
+            if (partial) {  // exact integer adds: the order of the contributors is free
+              if (rvalid) {
+                long long* const sks = sk_slot();
+#pragma unroll
+                for (int j = 0; j < C2; ++j)
+                  atomicAdd((unsigned long long*)(sks + (int64_t)(c0 + j) * kBM),
+                            (unsigned long long)acc[j]);
+              }
+              return;
+            }
+            store_c(acc, c0);
           };
           // Sa holds chunk 0 of this pair when it is not the first (loaded at
           // the end of the previous pair); chunks alternate between Sa and Sb.
@@ -634,12 +703,51 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
           else mbar_arrive(&acce[buf]);
         }
         if (g.stats && warp == 2 && lane == 0) {
-          const long long e2 = clock64();
+          const uint32_t e2 = (uint32_t)clock64();
           ep_wait += e1 - e0;
           ep_busy += e2 - e1;
           ++ep_pairs;
         }
         ++acc_it;
+        if constexpr (S8 && Cfg::GSTATE) {
+          if (partial && last) {
+            // This CTA's share of the split tile is in sk_sum; the last of the
+            // tile's contributors reads the total back and writes C.
+            const int tr = t - g.dp_tiles;
+            __threadfence();  // this thread's adds are performed before the count
+            named_bar(1, NE);
+            if (etid == 0) {
+              const unsigned prev = atomicAdd(&g.sk_count[tr * 2 + rank], 1u);
+              s_sk_last = (int)(prev + 1 == (unsigned)g.sk_chunks);
+            }
+            named_bar(1, NE);
+            if (s_sk_last) {
+              __threadfence();
+              constexpr int C2 = 16;
+              const long long* const sks = sk_slot();
+              // (Sa is free here: the next item starts with its first pair.)
+#pragma unroll 1
+              for (int c0 = cbeg; c0 < cbeg + Cfg::EPI_COLS; c0 += C2) {
+#pragma unroll
+                for (int j = 0; j < C2; ++j) Sa[j] = ld_cg_s64(sks + (int64_t)(c0 + j) * kBM);
+                if (!rvalid) continue;
+#pragma unroll
+                for (int j = 0; j < C2; ++j) {
+                  const int64_t col = col0 + c0 + j;
+                  if (col >= g.M) continue;
+                  double v = g.alpha * fixed_value(Sa[j], eA0 + s_eB[c0 + j] + g.fix_scale);
+                  if (g.beta != 0.0) v = fma(g.beta, g.Cin[row * g.ldcin + col], v);
+                  if (!g.symmetric) {
+                    g.C[row * g.ldc + col] = v;
+                  } else if (tm != tn || col >= row) {
+                    g.C[row * g.ldc + col] = v;
+                    g.C[col * g.ldc + row] = v;
+                  }
+                }
+              }
+            }
+          }
+        }
       }
     }
     if (g.stats && warp == 2 && lane == 0) {
@@ -706,6 +814,17 @@ static int group_m_rows() {
   return v;
 }
 
+// Pair split of the last partial wave of int8 wide tiles (OZK_GEMM_SPLIT,
+// default on; 0 deals whole tiles round-robin only).
+static bool split_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("OZK_GEMM_SPLIT");
+    v = (s && s[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 // CTA-pair tiles are the default for wide outputs; OZK_GEMM_PAIR=0 selects
 // single-CTA tiles (kept for comparison and as a fallback).
 static bool pair_mode_enabled() {
@@ -764,7 +883,8 @@ static int launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const PairLis
   const int sms = device_sm_count(dev);
   const int per = PAIR ? 2 : 1;
   const int max_units = sms / per;
-  const int units = ga.num_tiles < max_units ? ga.num_tiles : max_units;
+  const int units = (ga.num_tiles < max_units && ga.dp_tiles == ga.num_tiles) ? ga.num_tiles
+                                                                             : max_units;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(units * per));
   cfg.blockDim = dim3(Cfg::THREADS);
@@ -789,13 +909,21 @@ static int launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const PairLis
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_slice_gemm launch", e);
 }
 
-// Per-CTA running sums of the 256-wide tiles, then a 256-byte header (the
-// pacing counter).
+// State scratch of the 256-wide tiles: the per-CTA running sums, a 4 KB
+// header (the pacing counter at 0, the split tiles' counters from 256), then
+// the split tiles' int64 sums, one 256 x 256 tile per CTA pair at most.  The
+// wide kernel needs the first two parts; the pair split needs all three.
 static size_t gemm_state_sums_bytes(int dev) {
   return (size_t)device_sm_count(dev) * GemmCfg<256, true>::STATE_PER_CTA * sizeof(double);
 }
+static constexpr size_t kStateHeader = 4096;
+static constexpr size_t kSkCountOffset = 256;
+static size_t gemm_split_bytes(int dev) {
+  return (size_t)(device_sm_count(dev) / 2) * 2 * GemmCfg<256, true>::STATE_PER_CTA * sizeof(long long);
+}
+static size_t gemm_state_base_bytes(int dev) { return gemm_state_sums_bytes(dev) + kStateHeader; }
 
-size_t gemm_state_bytes(int dev) { return gemm_state_sums_bytes(dev) + 256; }
+size_t gemm_state_bytes(int dev) { return gemm_state_base_bytes(dev) + gemm_split_bytes(dev); }
 
 // Pacing slack in pairs (OZK_GEMM_PACE, default 1; 0 = off).  Measured on
 // B200 at 8192^3 with int8 slices: slack 1 cuts the GEMM's DRAM reads from
@@ -858,7 +986,7 @@ bool slice_gemm_s8_eligible(int64_t N, int64_t M, int64_t k_pad, int mode, int r
   int dev;
   cudaGetDevice(&dev);
   return mode == OZK_ACC_FIXED && rho >= kS8MinRho && N >= 256 && M >= 256 && k_pad > 0 &&
-         k_pad % kS8KB == 0 && k_pad <= 65536 && state_bytes >= gemm_state_bytes(dev) &&
+         k_pad % kS8KB == 0 && k_pad <= 65536 && state_bytes >= gemm_state_base_bytes(dev) &&
          pair_mode_enabled();
 }
 
@@ -900,7 +1028,7 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
   // when no scratch is given; narrow single-CTA tiles for narrow outputs
   // (e.g. residual right-hand sides).
   const bool wide = s8 || (mode != OZK_ACC_PRODUCTS && N >= 256 && M >= 256 && state &&
-                          state_bytes >= gemm_state_bytes(dev) && pair_mode_enabled());
+                          state_bytes >= gemm_state_base_bytes(dev) && pair_mode_enabled());
   const int BN = wide ? 256 : (M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128)));
   const int bn = (symmetric && !wide) ? 128 : BN;
   const bool pair = wide || (!symmetric && bn == 128 && pair_mode_enabled());
@@ -959,7 +1087,31 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
       if (e != cudaSuccess) return set_cuda_error("cudaMemsetAsync(pace)", e);
     }
   }
-  if (s8) return launch_bn<256, true, true>(ma, mb, pl, ga, dev, stream);
+  ga.dp_tiles = ga.num_tiles;
+  if (s8) {
+    // Pair split of a sparse last wave of tiles (exact: the partial sums are
+    // integers), when the scratch holds the split tiles' sums: with r tiles
+    // left for U units, each is cut into U / r >= 2 chunks.  (A last wave
+    // more than half full stays whole: measured on B200, the gram at
+    // 65536 x 4096 lost 5% with it split.)
+    const int units = device_sm_count(dev) / 2;
+    const int rem = ga.num_tiles % units;
+    const int chunks = rem ? units / rem : 0;
+    if (split_enabled() && chunks >= 2 && n_pairs >= chunks && state_bytes >= gemm_state_bytes(dev)) {
+      ga.dp_tiles = ga.num_tiles - rem;
+      ga.sk_chunks = chunks;
+      char* hdr = reinterpret_cast<char*>(state) + gemm_state_sums_bytes(dev);
+      ga.sk_count = reinterpret_cast<unsigned int*>(hdr + kSkCountOffset);
+      ga.sk_sum = reinterpret_cast<long long*>(hdr + kStateHeader);
+      cudaError_t e = cudaMemsetAsync(ga.sk_count, 0, (size_t)rem * 2 * sizeof(unsigned int), stream);
+      if (e == cudaSuccess)
+        e = cudaMemsetAsync(ga.sk_sum, 0,
+                            (size_t)rem * 2 * GemmCfg<256, true>::STATE_PER_CTA * sizeof(long long),
+                            stream);
+      if (e != cudaSuccess) return set_cuda_error("cudaMemsetAsync(split sums)", e);
+    }
+    return launch_bn<256, true, true>(ma, mb, pl, ga, dev, stream);
+  }
   if (wide) return launch_bn<256, true>(ma, mb, pl, ga, dev, stream);
   switch (bn) {
     case 16: return launch_bn<16, false>(ma, mb, pl, ga, dev, stream);

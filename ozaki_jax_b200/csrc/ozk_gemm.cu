@@ -80,12 +80,13 @@ struct GemmArgs {
   uint64_t pace_budget_ns;
   // Work split (int8 wide tiles): tiles below dp_tiles go round-robin, whole;
   // each of the r remaining tiles is cut into sk_chunks equal pair ranges, and
-  // unit u < r * sk_chunks takes chunk u / r of tile dp_tiles + u % r, so the
-  // units on one chunk run the same pairs of neighbouring tiles at once (their
-  // panels are shared in L2, as in the whole-tile waves).  A unit holding part
-  // of a tile's pairs adds its exact int64 partial sums into sk_sum and counts
-  // itself in sk_count; the last one to arrive writes C.  dp_tiles ==
-  // num_tiles: no split.
+  // the r * sk_chunks items j = (chunk j / r of tile dp_tiles + j % r) go
+  // round-robin too, so the units of a round run the same pairs of
+  // neighbouring tiles at once (their panels are shared in L2, as in the
+  // whole-tile waves).  A unit holding part of a tile's pairs adds its exact
+  // int64 partial sums into sk_sum and counts itself in sk_count; the last of
+  // the tile's sk_chunks contributors writes C.  dp_tiles == num_tiles: no
+  // split.
   int dp_tiles, sk_chunks;
   long long* sk_sum;       // [tile - dp_tiles][rank][column][row in CTA]
   unsigned int* sk_count;  // [tile - dp_tiles][rank]
@@ -140,8 +141,8 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& tm, i
   tn = r / gsz;
 }
 
-// The work items of a unit: its round-robin whole tiles (ndp), then at most
-// one chunk of a split tile (nsk).
+// The work items of a unit: its round-robin whole tiles (ndp), then its
+// round-robin chunks of split tiles (nsk).
 struct ItemRange {
   int ndp, nsk;
 };
@@ -149,7 +150,8 @@ struct ItemRange {
 __device__ __forceinline__ ItemRange item_range(const GemmArgs& g, int unit, int n_units) {
   ItemRange r;
   r.ndp = g.dp_tiles > unit ? (g.dp_tiles - unit + n_units - 1) / n_units : 0;
-  r.nsk = unit < (g.num_tiles - g.dp_tiles) * g.sk_chunks ? 1 : 0;
+  const int items = (g.num_tiles - g.dp_tiles) * g.sk_chunks;
+  r.nsk = items > unit ? (items - unit + n_units - 1) / n_units : 0;
   return r;
 }
 
@@ -163,8 +165,9 @@ __device__ __forceinline__ void item_at(const GemmArgs& g, const ItemRange& r, i
     return;
   }
   const int rem = g.num_tiles - g.dp_tiles;
-  const int chunk = unit / rem;
-  t = g.dp_tiles + unit % rem;
+  const int j = unit + (i - r.ndp) * n_units;  // split item
+  const int chunk = j / rem;
+  t = g.dp_tiles + j % rem;
   p0 = chunk * np / g.sk_chunks;
   p1 = (chunk + 1) * np / g.sk_chunks;
 }
@@ -317,9 +320,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
       if (g.pace && (!PAIR || rank == 0)) {
         // A unit with fewer tiles (or one that stopped) counts as done with
         // every pair the longest walk has, so no one waits for it.
+        const int items = (g.num_tiles - g.dp_tiles) * g.sk_chunks;
         const long long longest =
             (long long)((g.dp_tiles + n_units - 1) / n_units) * npairs +
-            (g.dp_tiles < g.num_tiles ? (npairs + g.sk_chunks - 1) / g.sk_chunks : 0);
+            (items ? (long long)((items + n_units - 1) / n_units) *
+                         ((npairs + g.sk_chunks - 1) / g.sk_chunks)
+                   : 0);
         if (longest > walk) atomicAdd(g.pace, (unsigned long long)(longest - walk));
       }
       if (g.stats) g.stats[8 * blockIdx.x + 2] = (unsigned long long)w_empty;
@@ -1089,15 +1095,28 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
   }
   ga.dp_tiles = ga.num_tiles;
   if (s8) {
-    // Pair split of a sparse last wave of tiles (exact: the partial sums are
-    // integers), when the scratch holds the split tiles' sums: with r tiles
-    // left for U units, each is cut into U / r >= 2 chunks.  (A last wave
-    // more than half full stays whole: measured on B200, the gram at
-    // 65536 x 4096 lost 5% with it split.)
+    // Pair split of the last wave of tiles (exact: the partial sums are
+    // integers), when the scratch holds the split tiles' sums.  With r tiles
+    // left for U units, chunks of 1/k of a tile's pairs take ceil(r k / U) / k
+    // of a tile's time instead of one: the k <= 8 that minimises it (the
+    // smallest on ties), if that saves at least a tenth.  (Splitting every
+    // tile into one chunk per pair-item share, with the units on different
+    // pairs at once, lost 5% at the 65536 x 4096 gram: no panel reuse.)
     const int units = device_sm_count(dev) / 2;
     const int rem = ga.num_tiles % units;
-    const int chunks = rem ? units / rem : 0;
-    if (split_enabled() && chunks >= 2 && n_pairs >= chunks && state_bytes >= gemm_state_bytes(dev)) {
+    int chunks = 1;
+    if (rem) {
+      double best = 1.0;
+      for (int k = 2; k <= 8 && k <= n_pairs; ++k) {
+        const double cost = (double)((rem * k + units - 1) / units) / k;
+        if (cost < best - 1e-9) {
+          best = cost;
+          chunks = k;
+        }
+      }
+      if (best > 0.9) chunks = 1;
+    }
+    if (split_enabled() && chunks >= 2 && state_bytes >= gemm_state_bytes(dev)) {
       ga.dp_tiles = ga.num_tiles - rem;
       ga.sk_chunks = chunks;
       char* hdr = reinterpret_cast<char*>(state) + gemm_state_sums_bytes(dev);

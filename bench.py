@@ -59,6 +59,54 @@ def peaks():
     return 1400.0, 6650.0, "fallback"
 
 
+def int8_peak(dev, seconds=1.5):
+    """Sustained int8 x int8 -> int32 GEMM rate of cuBLASLt (torch._int_mm) on
+    this GPU: 8192^3 looped for about `seconds`, so under the same power cap as
+    the slice GEMM -- the int8 counterpart of the measured BF16 peak, which
+    MEASURED_PEAKS.json does not have.  Returns (TOP/s or None, source text)."""
+    import torch
+
+    try:
+        n = 8192
+        g = torch.Generator(device=dev)
+        g.manual_seed(1)
+        a = torch.randint(-64, 64, (n, n), dtype=torch.int8, device=dev, generator=g)
+        b = torch.randint(-64, 64, (n, n), dtype=torch.int8, device=dev, generator=g).t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        iters = max(10, int(seconds * 1e3 / (e0.elapsed_time(e1) / 10)))
+        e0.record()
+        for _ in range(iters):
+            torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / iters
+        return (2.0 * n ** 3 / (ms * 1e-3) / 1e12,
+                f"cuBLASLt int8 GEMM (torch._int_mm) {n}^3, {iters} calls "
+                f"({iters * ms / 1e3:.1f} s sustained), measured in this run")
+    except Exception as e:  # noqa: BLE001 -- report, fall back to the BF16-derived figure
+        return None, f"int8 GEMM unavailable ({type(e).__name__})"
+
+
+def tensor_peak(s8, dev):
+    """(peak, unit, source, extra fields) for the slice GEMM's roofline.  The
+    int8 peak is 2x the BF16 one (NVIDIA's dense int8 rate is twice its BF16
+    rate); cuBLASLt's own int8 GEMM, timed here as well, reaches less than
+    that on B200, so it is reported beside it as context only."""
+    bf16_peak, _, src = peaks()
+    if not s8:
+        return bf16_peak, "TFLOP/s", f"{src} sustained bf16", {}
+    p, why = int8_peak(dev)
+    return 2.0 * bf16_peak, "TOP/s", f"2x {src} sustained bf16 (int8 dense rate)", {
+        "int8_library_gemm": p, "int8_library_gemm_source": why}
+
+
 def make_inputs(n, k, m):
     rng = np.random.RandomState(0)
     A = rng.randn(n, k)
@@ -410,11 +458,7 @@ def ours(args):
     if rank == 0:
         bf16_peak, hbm_peak, src = peaks()
         gemm_tflops = npairs * 2.0 * nb * k * m / (gemm_ms * 1e-3) / 1e12
-        # int8 MMAs run at twice the BF16 rate on B200; MEASURED_PEAKS.json has
-        # no int8 figure, so the int8 peak is stated as 2x the measured BF16 one
-        mma_peak = 2.0 * bf16_peak if s8 else bf16_peak
-        peak_src = (f"2x {src} sustained bf16 (int8 dense rate; no int8 measurement)" if s8
-                    else f"{src} sustained bf16")
+        mma_peak, mma_unit, peak_src, peak_extra = tensor_peak(s8, dev)
         ext_bytes = (8.0 * (nb * k + k * m) + (1.0 if s8 else 2.0) * nS * (nb + m) * k_pad
                      + 4.0 * nS * (nb + m))
         cpu_v, cpu_rows, cpu_dt = cpu_oracle_sample(A, B, n_hi, n_lo)
@@ -435,9 +479,11 @@ def ours(args):
             "gemm_wait_fractions": gemm_waits,
             "roofline": {"bound": "tensor", "kernel": "k_slice_gemm",
                          "mma": "int8 x int8 -> int32" if s8 else "bf16 x bf16 -> fp32",
-                         "achieved": gemm_tflops, "peak": mma_peak,
-                         "unit": "TOP/s" if s8 else "TFLOP/s",
-                         "frac": gemm_tflops / mma_peak, "peak_source": peak_src,
+                         "achieved": gemm_tflops, "peak": mma_peak, "unit": mma_unit,
+                         "frac": gemm_tflops / mma_peak, "peak_source": peak_src, **peak_extra,
+                         "frac_of_int8_library_gemm": (gemm_tflops / peak_extra["int8_library_gemm"]
+                                                       if peak_extra.get("int8_library_gemm")
+                                                       else None),
                          "traffic": GEMM_TRAFFIC_BYTES.get(
                              (n, args.precision, "int8" if s8 else "bf16")) if world == 1 else None,
                          "traffic_unit": "bytes per launch (ncu dram__bytes_read+write)",
@@ -562,11 +608,12 @@ def other_workload(args):
             # only the tiles on or above the diagonal are computed
             tiles = (k // 256) * (k // 256 + 1) / 2 / (k // 256) ** 2
             tensor *= tiles
-        peak = 2 * bf16_peak if s8 else bf16_peak
-        out["roofline"] = {"bound": "tensor", "achieved": tensor / (ms * 1e-3) / 1e12, "peak": peak,
-                           "unit": "TOP/s" if s8 else "TFLOP/s",
-                           "frac": tensor / (ms * 1e-3) / 1e12 / peak,
-                           "peak_source": ("2x " if s8 else "") + f"{src} sustained bf16"}
+        peak, unit, psrc, extra = tensor_peak(s8, dev)
+        ach = tensor / (ms * 1e-3) / 1e12
+        out["roofline"] = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": unit,
+                           "frac": ach / peak, "peak_source": psrc, **extra}
+        if extra.get("int8_library_gemm"):
+            out["roofline"]["frac_of_int8_library_gemm"] = ach / extra["int8_library_gemm"]
     print(json.dumps(out), flush=True)
 
 

@@ -66,6 +66,20 @@ def test_blocked_equals_device_pipeline(mode, block_rows):
     assert np.array_equal(C.view(np.int64), R.view(np.int64))
 
 
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("K", [300, 4224])  # BF16 slices; int8 codes (rho 19)
+def test_uneven_row_blocks(mode, K):
+    # N = 1100 -> row blocks of 768 and 332 (a short last block): every block's
+    # extraction and GEMM give exactly the rows of the whole product
+    rng = np.random.RandomState(11)
+    A = rng.randn(1100, K) * np.exp(rng.randn(1100, 1))
+    B = rng.randn(K, 1300) * np.exp(rng.randn(1, 1300))
+    C, flags = hostbuf(A, B, 4, 1, mode)
+    assert flags == 0
+    R = device_result(A, B, 4, 1, mode)
+    assert np.array_equal(C.view(np.int64), R.view(np.int64))
+
+
 def test_strided_and_pinned_host_arrays():
     rng = np.random.RandomState(4)
     Abig = rng.randn(700, 260)

@@ -617,6 +617,55 @@ def other_workload(args):
     print(json.dumps(out), flush=True)
 
 
+def kernel_case(spec, steps):
+    """One small case of a single hot kernel, for profiling (the ncu captures
+    summarised under profiles/ run these): 'extract:ROWSxK' runs the int8 row
+    extraction (ozk_extract_rows_s8_f64, preset high) on N(0,1) rows,
+    'residual:ROWSxK' runs residual(mode='ozaki') with 16 right-hand sides.
+    Prints one JSON line with the mean time of `steps` calls after one."""
+    import torch
+
+    import ozaki_jax_b200 as oz
+    from ozaki_jax_b200 import _lib
+
+    kind, shape = spec.split(":")
+    n, k = (int(v) for v in shape.lower().split("x"))
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    A = torch.randn(n, k, generator=g, device=dev, dtype=torch.float64)
+    if kind == "extract":
+        lib = _lib.load()
+        k8 = (k + 127) // 128 * 128
+        SA = torch.empty((5, n, k8), dtype=torch.int8, device=dev)
+        eA = torch.empty((5, n), dtype=torch.int32, device=dev)
+        fail = torch.zeros(1, dtype=torch.int32, device=dev)
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        rho = lib.ozk_compute_rho_f32(k)
+
+        def call():
+            _lib.check(lib.ozk_extract_rows_s8_f64(
+                A.data_ptr(), k, n, k, rho, 4, 1, SA.data_ptr(), k8, eA.data_ptr(),
+                fail.data_ptr(), st.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    elif kind == "residual":
+        x = torch.randn(k, 16, generator=g, device=dev, dtype=torch.float64)
+        b = torch.randn(n, 16, generator=g, device=dev, dtype=torch.float64)
+
+        def call():
+            oz.residual(A, x, b, mode="ozaki")
+    else:
+        raise SystemExit(f"unknown case {spec!r}")
+    call()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"case": spec, "ms": e0.elapsed_time(e1) / steps, "steps": steps}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -633,8 +682,13 @@ def main():
     ap.add_argument("--workload", choices=["c2"] + sorted(WORKLOADS), default="c2",
                     help="c2 (default): the headline 8192^3 line; others: the remaining "
                          "BASELINE configurations on one GPU")
+    ap.add_argument("--case", default=None,
+                    help="profiling aid, not a bench line: one small single-kernel case, "
+                         "extract:ROWSxK or residual:ROWSxK (--steps calls after one)")
     args = ap.parse_args()
-    if args.workload != "c2" and args.impl == "ours":
+    if args.case:
+        kernel_case(args.case, args.steps)
+    elif args.workload != "c2" and args.impl == "ours":
         other_workload(args)
     elif args.impl == "reference":
         reference_arm(args)

@@ -46,8 +46,8 @@ PRESETS = {"high": (4, 1), "medium": (3, 1), "max": (5, 4)}
 # from one capture of this command on a B200:
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none \
 #       -k regex:k_slice_gemm -c 1 python bench.py --steps 2 --warmup 1
-# (11.16 GB read + 0.51 GB written).  Other workloads report null.
-GEMM_TRAFFIC_BYTES = {(8192, "high", "int8"): 11.67e9}
+# (11.90 GB read + 0.70 GB written).  Other workloads report null.
+GEMM_TRAFFIC_BYTES = {(8192, "high", "int8"): 12.60e9}
 
 
 def peaks():

@@ -257,7 +257,7 @@ static int skinny_fixed(const double* A, int64_t lda, const double* B, int64_t l
     return rc;
   if ((rc = launch_skinny_s8((const int8_t*)w.SA, w.eA, (const int8_t*)w.SB, w.eB, nS, N, M, k8,
                              pa, pb, np, alpha, beta, Cin, ldcin, C, ldc, rho, status_dev, w.gate,
-                             0, s)))
+                             0, w.state, w.state_bytes, s)))
     return rc;
   if ((rc = launch_extract_rows_gated(A, lda, N, K, rho, n_hi, n_lo, w.SA, k_pad, w.eA, status_dev,
                                       w.gate, s)))

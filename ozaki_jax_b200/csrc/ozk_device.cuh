@@ -198,6 +198,13 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   return pol;
 }
 
+// 32-bit load served by L2, not L1: for data other SMs wrote with atomics.
+__device__ __forceinline__ int ld_cg_s32(const int* p) {
+  int v;
+  asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // 64-bit load served by L2, not L1: for data other SMs wrote with atomics.
 __device__ __forceinline__ long long ld_cg_s64(const long long* p) {
   long long v;

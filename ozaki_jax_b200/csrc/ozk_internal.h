@@ -91,7 +91,8 @@ int launch_skinny_s8(const int8_t* SA, const int32_t* eA, const int8_t* SX, cons
                      int nS, int64_t N, int64_t M, int64_t k8, const uint8_t* pair_a,
                      const uint8_t* pair_b, int n_pairs, double alpha, double beta,
                      const double* Cin, int64_t ldcin, double* C, int64_t ldc, int rho,
-                     int32_t* status, const int32_t* gate, int gate_want, cudaStream_t stream);
+                     int32_t* status, const int32_t* gate, int gate_want, void* scratch,
+                     size_t scratch_bytes, cudaStream_t stream);
 // int8 slices enabled (OZK_S8=0 in the environment turns them off).
 bool s8_enabled();
 // Tensor map over a [depth][rows][k_pad] slice stack (BF16, or int8 codes

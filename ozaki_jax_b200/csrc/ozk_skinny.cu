@@ -23,6 +23,13 @@
 // is 5 MMAs per k-step instead of 24, and each A tile is read from shared
 // memory once per run rather than once per pair (at N = 16 the A operand's
 // shared-memory reads, not the tensor math, bound an MMA).
+//
+// K split: when the tiles would leave SMs idle (fewer tiles than SMs, or a
+// last wave less than half full), each tile's K range is cut into ksplit
+// parts on different CTAs.  A part's int32 pair products are added into the
+// tile's slot in a scratch with red.add -- integer adds, so the totals are
+// exactly the products of the whole K range -- and the last of the tile's
+// parts to arrive runs the fixed-point epilogue on them: bit-identical results.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -72,6 +79,9 @@ struct SkArgs {
   uint64_t budget_ns;
   const int32_t* gate;  // if set, the kernel runs only when (*gate != 0) == gate_want
   int gate_want;
+  int ksplit;              // K parts per tile (1: no split)
+  int32_t* sk_sum;         // ksplit > 1: [tile][pair * 16 + column][row in tile] int32
+  unsigned int* sk_count;  // ksplit > 1: [tile] parts arrived
 };
 
 __global__ void __launch_bounds__(kSkThreads, 1)
@@ -91,10 +101,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   uint64_t* mma_done = acce + 1;
   uint32_t* s_tmem = (uint32_t*)(mma_done + 1);
   volatile int* s_abort = (volatile int*)(s_tmem + 1);
+  volatile int* s_sk_last = s_abort + 1;  // epilogue: this CTA completes a split tile
   auto a_tile = [&](int s, int a) { return smem + s * stage_bytes + a * kSkABytes; };
   auto x_tile = [&](int s, int b) { return smem + s * stage_bytes + nS * kSkABytes + b * kSkXBytes; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Work items j: tile j / ksplit, k-blocks [kb0(j), kb1(j)) of it.
+  const int n_items = g.num_tiles * g.ksplit;
+  auto kb0 = [&](int j) { return (j % g.ksplit) * g.num_kb / g.ksplit; };
+  auto kb1 = [&](int j) { return (j % g.ksplit + 1) * g.num_kb / g.ksplit; };
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSkMaxStages; ++i) {
       mbar_init(&full[i], 1);
@@ -119,8 +134,9 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       tma_prefetch_desc(&mapX);
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
-        for (int kb = 0; kb < g.num_kb; ++kb) {
+      for (int j = blockIdx.x; ok && j < n_items; j += gridDim.x) {
+        const int t = j / g.ksplit;
+        for (int kb = kb0(j); kb < kb1(j); ++kb) {
           const uint32_t s = it % ST, ph = (it / ST) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, s_abort, g.status, g.budget_ns)) {
             ok = false;
@@ -146,10 +162,11 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       constexpr uint32_t idesc0 = umma_idesc_s8(kSkRows, 0);
       uint32_t it = 0, tile_it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x, ++tile_it) {
+      for (int j = blockIdx.x; ok && j < n_items; j += gridDim.x, ++tile_it) {
         if (!mbar_wait(acce, (tile_it & 1) ^ 1, s_abort, g.status, g.budget_ns)) break;
         tc_fence_after();
-        for (int kb = 0; kb < g.num_kb; ++kb) {
+        const int kbf = kb0(j);
+        for (int kb = kbf; kb < kb1(j); ++kb) {
           const uint32_t s = it % ST, ph = (it / ST) & 1;
           if (!mbar_wait(&full[s], ph, s_abort, g.status, g.budget_ns)) {
             ok = false;
@@ -165,7 +182,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
 #pragma unroll
             for (int kk = 0; kk < kS8KB / 32; ++kk)
               umma_s8(tmem + p0 * kSkCols, umma_desc_sw128(a0 + kk * 32),
-                      umma_desc_sw128(x0 + kk * 32), idesc, (kb | kk) != 0);
+                      umma_desc_sw128(x0 + kk * 32), idesc, ((kb - kbf) | kk) != 0);
           }
           umma_commit(&empty[s]);
           ++it;
@@ -191,14 +208,41 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     for (int e = et + kSkCols; e < nS * kSkCols; e += 128) s_eX[e] -= s_eX[e % kSkCols];
     named_bar(1, 128);
     uint32_t tile_it = 0;
-    for (int t = blockIdx.x; t < g.num_tiles; t += gridDim.x, ++tile_it) {
+    for (int j = blockIdx.x; j < n_items; j += gridDim.x, ++tile_it) {
+      const int t = j / g.ksplit;
       int got = 1;
       if (lane == 0) got = mbar_wait(accf, tile_it & 1, s_abort, g.status, g.budget_ns);
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
       tc_fence_after();
-      const int64_t row = (int64_t)t * kSkRows + q * 32 + lane;
+      const int rq = q * 32 + lane;  // row within the tile
+      const int64_t row = (int64_t)t * kSkRows + rq;
       const bool rvalid = row < g.N;
+      const bool split = g.ksplit > 1;
+      int32_t* const slot = split ? g.sk_sum + (int64_t)t * pairs.n * kSkCols * kSkRows + rq : nullptr;
+      if (split) {
+        // This part's products into the tile's slot (exact int32 adds), the
+        // accumulators released, then the count; the last part goes on.
+        for (int p = 0; p < pairs.n; ++p) {
+          uint32_t P[kSkCols];
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + p * kSkCols, P);
+          tmem_wait_ld();
+          if (rvalid) {
+#pragma unroll
+            for (int c = 0; c < kSkCols; ++c)
+              if (c < g.M) atomicAdd(slot + (p * kSkCols + c) * kSkRows, (int)P[c]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce);
+        __threadfence();  // this thread's adds are performed before the count
+        named_bar(1, 128);
+        if (et == 0) *s_sk_last = (int)(atomicAdd(&g.sk_count[t], 1u) + 1 == (unsigned)g.ksplit);
+        named_bar(1, 128);
+        if (!*s_sk_last) continue;
+        __threadfence();
+      }
       const int eA0 = rvalid ? g.eA[row] : 0;
       long long acc[kSkCols];
 #pragma unroll
@@ -207,16 +251,23 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         const int a = pairs.a[p], b = pairs.b[p];
         const int ta = (rvalid ? g.eA[(int64_t)a * g.N + row] : 0) - eA0 + kFixFrac;
         uint32_t P[kSkCols];
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + p * kSkCols, P);
-        tmem_wait_ld();
+        if (split) {
+#pragma unroll
+          for (int c = 0; c < kSkCols; ++c) P[c] = (uint32_t)ld_cg_s32(slot + (p * kSkCols + c) * kSkRows);
+        } else {
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + p * kSkCols, P);
+          tmem_wait_ld();
+        }
 #pragma unroll
         for (int c = 0; c < kSkCols; ++c)
           acc[c] += fixed_term_s32((int32_t)P[c], ta + (b == 0 ? 0 : s_eX[b * kSkCols + c]));
       }
-      // The accumulators are read: the next tile's MMAs may start.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acce);
+      if (!split) {
+        // The accumulators are read: the next tile's MMAs may start.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acce);
+      }
       if (rvalid) {
 #pragma unroll
         for (int c = 0; c < kSkCols; ++c) {
@@ -250,7 +301,8 @@ int launch_skinny_s8(const int8_t* SA, const int32_t* eA, const int8_t* SX, cons
                      int nS, int64_t N, int64_t M, int64_t k8, const uint8_t* pair_a,
                      const uint8_t* pair_b, int n_pairs, double alpha, double beta,
                      const double* Cin, int64_t ldcin, double* C, int64_t ldc, int rho,
-                     int32_t* status, const int32_t* gate, int gate_want, cudaStream_t stream) {
+                     int32_t* status, const int32_t* gate, int gate_want, void* scratch,
+                     size_t scratch_bytes, cudaStream_t stream) {
   if (N == 0 || M == 0) return OZK_OK;
   if (!skinny_s8_eligible(N, M, k8, nS, n_pairs, rho))
     return set_error(OZK_ERR_UNSUPPORTED,
@@ -329,8 +381,39 @@ int launch_skinny_s8(const int8_t* SA, const int32_t* eA, const int8_t* SX, cons
   ga.budget_ns = wait_budget_ns();
   ga.gate = gate;
   ga.gate_want = gate_want;
-  int grid = device_sm_count(dev);
-  if (grid > ga.num_tiles) grid = ga.num_tiles;
+  // K split (exact, see the kernel) when the tiles would leave SMs idle: fewer
+  // tiles than SMs, or a last wave under half full.  The k <= 8 parts (each
+  // at least 4 k-blocks) minimise the rounds of work per part,
+  // ceil(tiles k / SMs) / k, if that saves at least a tenth.  (A last wave
+  // more than half full stays whole: the kernel streams from HBM, and the SMs
+  // of such a wave already draw most of its bandwidth.)
+  const int sms = device_sm_count(dev);
+  const int T = ga.num_tiles;
+  ga.ksplit = 1;
+  if (T < sms || T % sms < sms / 2) {
+    const double one = (double)((T + sms - 1) / sms);
+    double best = one;
+    int ks = 1;
+    for (int k = 2; k <= 8 && ga.num_kb / k >= 4; ++k) {
+      const double cost = (double)((T * k + sms - 1) / sms) / k;
+      if (cost < best - 1e-9) {
+        best = cost;
+        ks = k;
+      }
+    }
+    const size_t counts = ((size_t)T * sizeof(unsigned int) + 255) & ~(size_t)255;
+    const size_t sums = (size_t)T * n_pairs * kSkCols * kSkRows * sizeof(int32_t);
+    if (ks > 1 && best <= 0.9 * one && scratch && scratch_bytes >= counts + sums &&
+        ((uintptr_t)scratch & 255) == 0) {
+      ga.ksplit = ks;
+      ga.sk_count = (unsigned int*)scratch;
+      ga.sk_sum = (int32_t*)((char*)scratch + counts);
+      cudaError_t e = cudaMemsetAsync(scratch, 0, counts + sums, stream);
+      if (e != cudaSuccess) return set_cuda_error("cudaMemsetAsync(skinny split sums)", e);
+    }
+  }
+  int grid = sms;
+  if (grid > T * ga.ksplit) grid = T * ga.ksplit;
   k_skinny_s8<<<grid, kSkThreads, smem, stream>>>(ma, mx, pl, ga);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? OZK_OK : set_cuda_error("k_skinny_s8 launch", e);

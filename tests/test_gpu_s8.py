@@ -251,10 +251,14 @@ def residual_pipeline(A, X, Bv, n_hi, n_lo):
 
 
 @pytest.mark.parametrize("N,K,M,n_hi,n_lo", [(1000, 5000, 16, 4, 1), (300, 4224, 5, 4, 1),
-                                             (777, 6000, 1, 3, 1), (256, 8192, 16, 4, 2)])
+                                             (777, 6000, 1, 3, 1), (256, 8192, 16, 4, 2),
+                                             (19200, 4224, 16, 4, 1)])
 def test_skinny_s8_residual_matches_bf16(N, K, M, n_hi, n_lo):
     """Residuals (at most 16 right-hand sides) take the int8 all-pairs kernel;
-    bit-identical to the BF16 narrow kernel's fixed-point result."""
+    bit-identical to the BF16 narrow kernel's fixed-point result.  With fewer
+    128-row tiles than SMs (the small cases), or 150 tiles on a 148-SM B200,
+    each tile's K range is split over several CTAs and the int32 products
+    added in a scratch before the fixed-point sums."""
     rng = np.random.RandomState(N + M)
     A = rng.randn(N, K) * np.exp(rng.randn(N, 1) * 2)
     X, Bv = rng.randn(K, M), rng.randn(N, M)

@@ -621,8 +621,10 @@ def kernel_case(spec, steps):
     """One small case of a single hot kernel, for profiling (the ncu captures
     summarised under profiles/ run these): 'extract:ROWSxK' runs the int8 row
     extraction (ozk_extract_rows_s8_f64, preset high) on N(0,1) rows,
-    'residual:ROWSxK' runs residual(mode='ozaki') with 16 right-hand sides.
-    Prints one JSON line with the mean time of `steps` calls after one."""
+    'cols:KxCOLS' runs the int8 column extraction (ozk_extract_cols_s8_f64,
+    preset high) of a K x COLS operand, 'residual:ROWSxK' runs
+    residual(mode='ozaki') with 16 right-hand sides.  Prints one JSON line with
+    the mean time of `steps` calls after one."""
     import torch
 
     import ozaki_jax_b200 as oz
@@ -647,6 +649,22 @@ def kernel_case(spec, steps):
             _lib.check(lib.ozk_extract_rows_s8_f64(
                 A.data_ptr(), k, n, k, rho, 4, 1, SA.data_ptr(), k8, eA.data_ptr(),
                 fail.data_ptr(), st.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    elif kind == "cols":
+        # A is K x COLS here: n = K, k = COLS
+        lib = _lib.load()
+        k8 = (n + 127) // 128 * 128
+        SB = torch.empty((5, k, k8), dtype=torch.int8, device=dev)
+        eB = torch.empty((5, k), dtype=torch.int32, device=dev)
+        BT = torch.empty((k, n), dtype=torch.float64, device=dev)  # transposed-operand scratch
+        fail = torch.zeros(1, dtype=torch.int32, device=dev)
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        rho = lib.ozk_compute_rho_f32(n)
+
+        def call():
+            _lib.check(lib.ozk_extract_cols_s8_f64(
+                A.data_ptr(), k, n, k, rho, 4, 1, SB.data_ptr(), k8, eB.data_ptr(),
+                BT.data_ptr(), BT.numel() * 8, fail.data_ptr(), st.data_ptr(),
+                torch.cuda.current_stream().cuda_stream))
     elif kind == "residual":
         x = torch.randn(k, 16, generator=g, device=dev, dtype=torch.float64)
         b = torch.randn(n, 16, generator=g, device=dev, dtype=torch.float64)
@@ -684,7 +702,8 @@ def main():
                          "BASELINE configurations on one GPU")
     ap.add_argument("--case", default=None,
                     help="profiling aid, not a bench line: one small single-kernel case, "
-                         "extract:ROWSxK or residual:ROWSxK (--steps calls after one)")
+                         "extract:ROWSxK, cols:KxCOLS or residual:ROWSxK (--steps calls "
+                         "after one)")
     args = ap.parse_args()
     if args.case:
         kernel_case(args.case, args.steps)

@@ -367,6 +367,14 @@ __device__ __forceinline__ float max3_abs(float m, float a, float b) {
   return d;
 }
 
+// max(|a|, |b|), NaN if either is NaN (a NaN must not hide behind its
+// finite neighbour in a packed pair).
+__device__ __forceinline__ float max_abs_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(fabsf(a)), "f"(fabsf(b)));
+  return d;
+}
+
 // PRESET = 16 n_hi + n_lo fixes the slice counts at compile time (the pass
 // loop unrolls, the lo residuals die after their last pass); 0 takes them
 // from the arguments.
@@ -489,7 +497,7 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         float2& lo = rl[2 * q + j];
         split_f64(x[2 * j], hi.x, lo.x);
         split_f64(x[2 * j + 1], hi.y, lo.y);
-        odd |= !(fmaxf(fabsf(hi.x), fabsf(hi.y)) <= 3.402823466e38f);
+        odd |= !(max_abs_nan(hi.x, hi.y) <= 3.402823466e38f);
         mh = max3_abs(mh, hi.x, hi.y);
         ml = max3_abs(ml, lo.x, lo.y);
       }

@@ -80,6 +80,19 @@ def test_uneven_row_blocks(mode, K):
     assert np.array_equal(C.view(np.int64), R.view(np.int64))
 
 
+@pytest.mark.parametrize("mode", [L.OZK_ACC_FIXED, L.OZK_ACC_F64])
+def test_automatic_blocks_full_height(mode):
+    # N = 8192 -> automatic blocks of 1024 rows, as in the 8192^3 benchmark
+    # (int8 codes at K = 4224): still the whole product's rows
+    rng = np.random.RandomState(12)
+    A = rng.randn(8192, 4224) * np.exp(rng.randn(8192, 1))
+    B = rng.randn(4224, 300) * np.exp(rng.randn(1, 300))
+    C, flags = hostbuf(A, B, 4, 1, mode)
+    assert flags == 0
+    R = device_result(A, B, 4, 1, mode)
+    assert np.array_equal(C.view(np.int64), R.view(np.int64))
+
+
 def test_strided_and_pinned_host_arrays():
     rng = np.random.RandomState(4)
     Abig = rng.randn(700, 260)

@@ -80,6 +80,57 @@ def test_codes_are_the_bf16_slices(axis, K, n_hi, n_lo):
     assert np.all(q[:, :, K:] == 0)
 
 
+@pytest.mark.parametrize("K,lines,n_hi,n_lo", [(6001, 301, 4, 1), (8192, 3, 3, 1),
+                                               (4500, 1, 4, 2), (7000, 600, 4, 1)])
+def test_column_codes_odd_counts(K, lines, n_hi, n_lo):
+    """Column codes for odd, single and many columns, with a zero column:
+    codes and exponents must be the BF16 column slices'."""
+    rng = np.random.RandomState(K + lines)
+    X = rng.randn(K, lines) * np.exp(rng.randn(K, lines) * 2)
+    X[:, lines // 2] = 0.0  # a zero column
+    rho = O.compute_rho_f32(K)
+    codes, k8, e8, fail = s8_slices(X, rho, n_hi, n_lo, 0)
+    assert fail == 0
+    S16, _, e16, _ = extract_device(torch.as_tensor(X).cuda(), rho, n_hi, n_lo, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(e8, e16)
+    vals = bf16_values(S16)[:, :, :K]
+    q = codes.cpu().numpy().astype(np.float64)
+    assert np.array_equal(q[:, :, :K], vals.astype(np.float64) * 2.0 ** (24 - rho))
+    assert np.all(q[:, :, K:] == 0)
+
+
+@pytest.mark.parametrize("axis", [1, 0])
+@pytest.mark.parametrize("bad,flag", [(np.nan, L.OZK_FLAG_NONFINITE),
+                                      (np.inf, L.OZK_FLAG_NONFINITE),
+                                      (1e300, L.OZK_FLAG_RANGE)])
+def test_int8_extraction_flags_one_bad_value(axis, bad, flag):
+    """One non-finite or out-of-range value among finite ones (its neighbour
+    in the same packed pair is finite) raises its flag in the status word."""
+    rng = np.random.RandomState(3)
+    X = rng.randn(64, 6000) if axis == 1 else rng.randn(6000, 64)
+    X[(5, 1001) if axis == 1 else (1001, 5)] = bad
+    lib = L.load()
+    Xd = torch.as_tensor(X).cuda()
+    lines, K = (X.shape if axis == 1 else X.shape[::-1])
+    k8 = (K + 127) // 128 * 128
+    codes = torch.empty((5, lines, k8), dtype=torch.int8, device="cuda")
+    exps = torch.empty((5, lines), dtype=torch.int32, device="cuda")
+    fail = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rho = O.compute_rho_f32(K)
+    if axis == 1:
+        L.check(lib.ozk_extract_rows_s8_f64(Xd.data_ptr(), K, lines, K, rho, 4, 1,
+                                            codes.data_ptr(), k8, exps.data_ptr(), fail.data_ptr(),
+                                            st.data_ptr(), stream()))
+    else:
+        L.check(lib.ozk_extract_cols_s8_f64(Xd.data_ptr(), lines, K, lines, rho, 4, 1,
+                                            codes.data_ptr(), k8, exps.data_ptr(), None, 0,
+                                            fail.data_ptr(), st.data_ptr(), stream()))
+    torch.cuda.synchronize()
+    assert int(st.item()) & flag
+
+
 def bf16_fixed_gemm(SA, eA, SB, eB, k_pad, N, M, rho, n_hi, n_lo, symmetric=0, alpha=1.0,
                     beta=0.0, Cin=None):
     lib = L.load()
@@ -194,16 +245,24 @@ def test_pipeline_takes_s8_and_matches_bf16():
     assert same(C, bf16_pipeline(A, B, 4, 1))
 
 
+@pytest.mark.parametrize("side", ["A row", "B column"])
 @pytest.mark.parametrize("scale", [2.0 ** -135, 2.0 ** 112])
-def test_unrepresentable_slices_fall_back_on_device(scale):
-    """A row whose slices leave the range the int8 codes cover: the extraction
-    flags it, the int8 GEMM is skipped and the gated BF16 recomputation gives
-    the BF16 path's result (non-finite where the reference's is)."""
+def test_unrepresentable_slices_fall_back_on_device(scale, side):
+    """A row of A (or a column of B) whose slices leave the range the int8
+    codes cover: the extraction flags it, the int8 GEMM is skipped and the
+    gated BF16 recomputation gives the BF16 path's result (non-finite where
+    the reference's is)."""
     rng = np.random.RandomState(9)
     A, B = rng.randn(300, 4200), rng.randn(4200, 280)
-    A[17] *= scale
+    if side == "A row":
+        A[17] *= scale
+    else:
+        B[:, 17] *= scale
     rho = O.compute_rho_f32(4200)
-    _, _, _, fail = s8_slices(A, rho, 4, 1, 1)
+    if side == "A row":
+        _, _, _, fail = s8_slices(A, rho, 4, 1, 1)
+    else:
+        _, _, _, fail = s8_slices(B, rho, 4, 1, 0)
     assert fail == 1
     C, _ = pipeline(A, B)
     assert same(C, bf16_pipeline(A, B, 4, 1))

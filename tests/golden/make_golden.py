@@ -194,6 +194,26 @@ def main():
             msgs[label] = None
         except ValueError as e:
             msgs[label] = str(e)
+    # gram / residual argument checks (gram.py:66-84, solve.py:56-75, :113-128)
+    one = np.ones
+    for label, fn, args, kw in (
+            ("gram_bad_mode", oj.gram, (one((4, 4)),), dict(mode="invalid")),
+            ("gram_bad_accumulation", oj.gram, (one((4, 4)),), dict(mode="ozaki", accumulation="host")),
+            ("gram_not_2d", oj.gram, (one(4),), dict(mode="ozaki")),
+            ("residual_bad_mode", oj.residual, (one((3, 4)), one(4), one(3)), dict(mode="invalid")),
+            ("residual_bad_accumulation", oj.residual, (one((3, 4)), one(4), one(3)),
+             dict(mode="ozaki", accumulation="host")),
+            ("residual_not_2d", oj.residual, (one(4), one(4), one(4)), dict(mode="ozaki")),
+            ("residual_x_length", oj.residual, (one((3, 4)), one(5), one(3)), dict(mode="ozaki")),
+            ("residual_b_vector", oj.residual, (one((3, 4)), one(4), one(4)), dict(mode="ozaki")),
+            ("residual_x_rows", oj.residual, (one((3, 4)), one((5, 2)), one((3, 2))), dict(mode="ozaki")),
+            ("residual_b_matrix", oj.residual, (one((3, 4)), one((4, 2)), one((3, 3))), dict(mode="ozaki")),
+            ("residual_x_ndim", oj.residual, (one((3, 4)), one((4, 1, 1)), one(3)), dict(mode="ozaki"))):
+        try:
+            fn(*args, **kw)
+            msgs[label] = None
+        except ValueError as e:
+            msgs[label] = str(e)
     meta["messages"] = msgs
     fb_A, fb_B = rng.randn(2, 10000), rng.randn(10000, 2)
     arrays["fallback/A"], arrays["fallback/B"] = fb_A, fb_B

@@ -47,6 +47,33 @@ def test_gram_residual_validation():
         oz.residual(rng.randn(3, 4), rng.randn(4, 1, 1), rng.randn(3), mode="ozaki")
 
 
+def test_gram_residual_messages_match_reference(golden):
+    """Every argument check of gram / residual raises the reference's exact text
+    (the reference's own messages, recorded by make_golden.py)."""
+    _, meta = golden
+    msgs = meta["messages"]
+    one = np.ones
+    cases = {
+        "gram_bad_mode": (oz.gram, (one((4, 4)),), dict(mode="invalid")),
+        "gram_bad_accumulation": (oz.gram, (one((4, 4)),), dict(mode="ozaki", accumulation="host")),
+        "gram_not_2d": (oz.gram, (one(4),), dict(mode="ozaki")),
+        "residual_bad_mode": (oz.residual, (one((3, 4)), one(4), one(3)), dict(mode="invalid")),
+        "residual_bad_accumulation": (oz.residual, (one((3, 4)), one(4), one(3)),
+                                      dict(mode="ozaki", accumulation="host")),
+        "residual_not_2d": (oz.residual, (one(4), one(4), one(4)), dict(mode="ozaki")),
+        "residual_x_length": (oz.residual, (one((3, 4)), one(5), one(3)), dict(mode="ozaki")),
+        "residual_b_vector": (oz.residual, (one((3, 4)), one(4), one(4)), dict(mode="ozaki")),
+        "residual_x_rows": (oz.residual, (one((3, 4)), one((5, 2)), one((3, 2))), dict(mode="ozaki")),
+        "residual_b_matrix": (oz.residual, (one((3, 4)), one((4, 2)), one((3, 3))), dict(mode="ozaki")),
+        "residual_x_ndim": (oz.residual, (one((3, 4)), one((4, 1, 1)), one(3)), dict(mode="ozaki")),
+    }
+    for label, (fn, args, kw) in cases.items():
+        assert msgs[label], label
+        with pytest.raises(ValueError) as ei:
+            fn(*args, **kw)
+        assert str(ei.value) == msgs[label], label
+
+
 def test_preflight_bound_reasons():
     from ozaki_jax_b200.matmul import _bound_reasons
     from ozaki_jax_b200.host import host_safety_reasons

@@ -1,4 +1,4 @@
-"""Benchmark of the on-device Ozaki matmul:
+"""Benchmark of the on-device Ozaki matmul, headline configuration (c2):
 C = A @ B, A, B 8192 x 8192 FP64 N(0,1) (RandomState(0): A then B),
 precision='high' (n_hi=4, n_lo=1, 24 slice GEMMs), accumulation='fused'.
 
@@ -518,9 +518,10 @@ WORKLOADS = {
 
 
 def other_workload(args):
-    """The other BASELINE configurations on one GPU, through the C entry points
-    on device arrays (inputs drawn on the device from a seeded torch generator
-    with the distributions BASELINE describes).  Prints one JSON line."""
+    """The other benchmark configurations (c3 'max' on wide-range entries, c4
+    gram, c5a 'medium' 32768^3, c5b residual) on one GPU, through the C entry
+    points on device arrays (inputs drawn on the device from a seeded torch
+    generator with each configuration's distribution).  Prints one JSON line."""
     import torch
     from ozaki_jax_b200 import _lib
 
@@ -699,7 +700,7 @@ def main():
                          "(0: the library's own choice)")
     ap.add_argument("--workload", choices=["c2"] + sorted(WORKLOADS), default="c2",
                     help="c2 (default): the headline 8192^3 line; others: the remaining "
-                         "BASELINE configurations on one GPU")
+                         "benchmark configurations on one GPU")
     ap.add_argument("--case", default=None,
                     help="profiling aid, not a bench line: one small single-kernel case, "
                          "extract:ROWSxK, cols:KxCOLS or residual:ROWSxK (--steps calls "

@@ -209,7 +209,7 @@ def test_accuracy_gate_256x8192x256(golden):
 
 
 def test_wide_range_max_preset_config_c3():
-    """BASELINE config 3 in miniature: precision 'max' on (U(0,1)-0.5)*exp(10 N(0,1))
+    """The wide-range 'max' workload in miniature: (U(0,1)-0.5)*exp(10 N(0,1))
     entries, K = 8192 (int8 codes, 256-wide tiles).  Per-row scaling truncates the
     small entries of a row, so the reference's own error is large (about 1e-6);
     'fused' must stay within 1.5x of the reference's matmul_numpy error against

@@ -1,6 +1,6 @@
 """matmul(pipeline='host') on the device: FP64 extraction bit-identical to the
 oracle of ozaki_jax/extract.py:21-103, triangular pairs, FP64 accumulation;
-the reference's CI pins and the BASELINE config-1 case."""
+the reference's CI pins and the 256 x 256, n_slices=8 CPU-plumbing case."""
 
 import numpy as np
 import pytest
@@ -78,7 +78,7 @@ def test_host_ci_pins():
 
 
 def test_config1_256_host_pipeline():
-    """256x256 N(0,1) seed 0, n_slices=8 -> ~5.6e-16."""
+    """The plumbing case: 256x256 N(0,1) seed 0, n_slices=8 -> ~5.6e-16."""
     rng = np.random.RandomState(0)
     A, B = rng.randn(256, 256), rng.randn(256, 256)
     E = O.exact_product(A, B)

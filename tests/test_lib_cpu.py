@@ -79,6 +79,64 @@ def test_argument_errors_return_codes():
     assert "NULL" in _lib.detail()
 
 
+def test_every_entry_point_checks_arguments_before_device_work():
+    """Each compute entry point refuses bad arguments with its status code
+    (never an exception, never a device call): NULL pointers, shapes, leading
+    dimensions, presets, the exact-product bound, workspace limits.  Empty
+    products return OZK_OK without touching the device."""
+    from ozaki_jax_b200 import _lib
+    lib = _lib.load()
+    ARG, UNSAFE, WS, OK = _lib.OZK_ERR_ARG, _lib.OZK_ERR_UNSAFE, _lib.OZK_ERR_WORKSPACE, _lib.OZK_OK
+    buf = (ctypes.c_double * 16)()
+    p = ctypes.addressof(buf)  # a host address: never dereferenced by these calls
+    big = 2 ** 23              # K beyond the FP32 extraction's exact-product bound
+    # matmul: shapes, leading dimensions, accumulation mode, preset, bound, empty
+    mm = lib.ozk_matmul_f64
+    assert mm(p, 4, p, 4, p, 4, 4, 0, 4, -1, 4, 1, 2, None, 0, None, None) == ARG
+    assert mm(p, 3, p, 4, p, 4, 4, 4, 4, -1, 4, 1, 2, None, 0, None, None) == ARG
+    assert mm(p, 4, p, 4, p, 4, 4, 4, 4, -1, 4, 1, 7, None, 0, None, None) == ARG
+    assert mm(p, 4, p, 4, p, 4, 4, 4, 4, -1, 0, 1, 2, None, 0, None, None) == ARG
+    assert mm(p, big, p, 4, p, 4, 4, big, 4, -1, 4, 1, 2, None, 0, None, None) == UNSAFE
+    assert mm(p, 4, p, 4, p, 4, 0, 4, 4, -1, 4, 1, 2, None, 0, None, None) == OK
+    # host-buffer matmul
+    hb = lib.ozk_matmul_f64_hostbuf
+    flags = ctypes.c_int32(0)
+    assert hb(None, 4, p, 4, p, 4, 4, 4, 4, -1, 4, 1, 2, 0, None, 0, ctypes.byref(flags),
+              None) == ARG
+    assert hb(p, 4, p, 4, p, 4, 4, 4, 4, -1, 4, 1, 9, 0, None, 0, ctypes.byref(flags),
+              None) == ARG
+    # allocation-free matmul: presets and its fixed scratch limit
+    na = lib.ozk_matmul_f64_noalloc
+    assert na(p, 4, p, 4, p, 4, 4, 4, 4, 0, 1, None, None) == ARG
+    assert na(p, 8192, p, 8192, p, 8192, 8192, 8192, 8192, 4, 1, None, None) == WS
+    # FP64 host pipeline: slice count, slice budget
+    hp = lib.ozk_matmul_host_f64
+    assert hp(p, 4, p, 4, p, 4, 4, 4, 4, -1, 0, None, 0, None, None) == ARG
+    assert hp(p, 4, p, 4, p, 4, 4, 4, 4, -1, 99, None, 0, None, None) == ARG
+    assert hp(p, 10000, p, 2, p, 2, 2, 10000, 2, -1, 8, None, 0, None, None) == UNSAFE
+    # gram and residual
+    gm = lib.ozk_gram_f64
+    assert gm(None, 4, p, 4, 4, 4, -1, 4, 1, None, 0, None, None) == ARG
+    assert gm(p, 4, p, 4, 0, 4, -1, 4, 1, None, 0, None, None) == ARG
+    assert gm(p, 4, p, 3, 4, 4, -1, 4, 1, None, 0, None, None) == ARG
+    assert gm(p, 4, p, 4, 4, 0, -1, 4, 1, None, 0, None, None) == OK
+    rs = lib.ozk_residual_f64
+    assert rs(p, 4, None, 2, p, 2, p, 2, 4, 4, 2, -1, 4, 1, None, 0, None, None) == ARG
+    assert rs(p, 4, p, 1, p, 2, p, 2, 4, 4, 2, -1, 4, 1, None, 0, None, None) == ARG
+    assert rs(p, 4, p, 2, p, 2, p, 2, 0, 4, 2, -1, 4, 1, None, 0, None, None) == OK
+    # accumulation and schedules
+    assert lib.ozk_accumulate_2sum(None, p, p, 4, 4, 4, 1, None, None, p, 4, None) == ARG
+    assert lib.ozk_accumulate_2sum(p, p, p, 4, 4, 0, 1, None, None, p, 4, None) == ARG
+    pa = (ctypes.c_uint8 * 4)()
+    pb = (ctypes.c_uint8 * 4)()
+    assert lib.ozk_triangular_schedule(0, pa, pb, 4) == ARG
+    assert lib.ozk_triangular_schedule(8, pa, pb, 4) == ARG  # 36 pairs do not fit in 4
+    # every refusal leaves a readable detail and a name for its code
+    assert _lib.detail()
+    for code in (ARG, UNSAFE, WS):
+        assert lib.ozk_strerror(code)
+
+
 def test_log2_table_matches_numpy_log2():
     """The device's exponent rule floor(RN32(log2 m)) (a per-binade threshold
     table) agrees with NumPy's float32 log2 -- the reference's rule,

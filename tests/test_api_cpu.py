@@ -103,3 +103,19 @@ def test_public_names_match_the_reference_hot_path():
                  "jax_extract_split_rows", "jax_extract_split_cols", "accumulate_2sum",
                  "validate_accumulation_2sum"):
         assert callable(getattr(oz, name)), name
+
+
+def test_no_cpu_fallback_without_a_device():
+    """With no CUDA device the product path raises instead of computing on the
+    host: valid calls of every public compute function fail loudly."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is visible")
+    A = np.ones((8, 8))
+    calls = [lambda: oz.matmul(A, A, pipeline="ondevice"),
+             lambda: oz.matmul(A, A, pipeline="host"),
+             lambda: oz.gram(A, mode="ozaki"),
+             lambda: oz.residual(A, np.ones(8), np.ones(8), mode="ozaki")]
+    for call in calls:
+        with pytest.raises(RuntimeError, match="needs a CUDA device"):
+            call()

@@ -3,24 +3,30 @@ C = A @ B, A, B 8192 x 8192 FP64 N(0,1) (RandomState(0): A then B),
 precision='high' (n_hi=4, n_lo=1, 24 slice GEMMs), accumulation='fused'.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c2|c3|c4|c5a|c5b]
     torchrun --nproc-per-node N bench.py --gpus N ...   (one rank per GPU)
 
-A step is one pass of the pipeline over one batch: split + slice extraction
-of A (row block) and B, then the persistent slice-pair GEMM with the FP64
-epilogue.  Multi-GPU: rank r owns rows [r N/P, (r+1) N/P) of A and C (the
-row extraction is row-local, so sharded slices are identical), B is given to
-every rank; total work is fixed (strong scaling), no collective sits in the
-data path; timing is the max over ranks.  Inputs (1 GiB) exceed L2, so no
-flush is needed between steps.
+A step is one call of the C-ABI operator a caller runs (ozk_matmul_f64 for
+matmul, ozk_gram_f64, ozk_residual_f64) on inputs resident in HBM: split and
+slice extraction of A and B, then the persistent slice-pair GEMM with the
+exact fixed-point epilogue, and every other launch the operator makes (the
+gated BF16 recomputation, which exits at once when the int8 codes were exact).
+The operator's kernels are also launched one by one in a second timed loop,
+for the per-kernel split and the roofline of the slice GEMM.  Multi-GPU:
+rank r owns rows [r N/P, (r+1) N/P) of A and C; timing is the max over ranks.
+Inputs exceed L2 (126 MB), so no flush is needed between steps.
 
 Rank 0 prints one JSON line.  `value` is FP64-equivalent TFLOP/s (2NKM/t)
-with inputs resident in HBM; `e2e` is the same metric through the public
-API (ozaki_jax_b200.matmul on pinned host NumPy arrays -> the C entry point
-ozk_matmul_f64_hostbuf, which overlaps the PCIe copies with the compute in
-row blocks), every copy inside the timed region;
-`cpu_baseline` times the NumPy oracle (the reference's
-matmul_numpy(pipeline='ondevice') restated) on a row sample on the host
-cores.  --impl reference runs only that CPU reference arm.
+of the operator; `parity` compares blocks of the full-size result with the
+reference's result on the same blocks of the same input (the NumPy oracle;
+rows of A and columns of B are extracted independently, so a block of the
+oracle's output is that block of the full reference result), both against the
+exact product; `e2e` is the same metric through the public API
+(ozaki_jax_b200.matmul / gram / residual) on ordinary pageable NumPy arrays,
+every copy inside the timed region (`pinned_value`: the same with page-locked
+inputs); `cpu_baseline` times the NumPy oracle (the reference's
+matmul_numpy(pipeline='ondevice') restated) on a block of the result with all
+host cores.  --impl reference runs only that CPU reference arm.
 """
 
 import argparse
@@ -105,13 +111,6 @@ def tensor_peak(s8, dev):
     p, why = int8_peak(dev)
     return 2.0 * bf16_peak, "TOP/s", f"2x {src} sustained bf16 (int8 dense rate)", {
         "int8_library_gemm": p, "int8_library_gemm_source": why}
-
-
-def make_inputs(n, k, m):
-    rng = np.random.RandomState(0)
-    A = rng.randn(n, k)
-    B = rng.randn(k, m)
-    return A, B
 
 
 class Clocks:
@@ -227,54 +226,235 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
-def cpu_oracle_sample(A, B, n_hi, n_lo, budget_s=12.0, max_rows=1024):
-    """Times the NumPy oracle on the first rows of A (row-local extraction
-    makes those rows exact oracle rows) and returns (FP64-equiv TFLOP/s,
-    rows, seconds)."""
+# ---------------------------------------------------------------------------
+# Workloads: BASELINE's configurations, drawn on the host from
+# np.random.RandomState(0) in the order written next to each
+# ---------------------------------------------------------------------------
+
+WORKLOADS = {
+    # name: (description, precision, kind)
+    "c2": ("matmul 8192^3 precision=high, N(0,1)", "high", "matmul"),
+    "c3": ("matmul 4096x8192x4096 precision=max, (U(0,1)-0.5)*exp(10*N(0,1)) entries", "max",
+           "matmul"),
+    "c4": ("gram A^T A, A 65536x4096 N(0,1), column j scaled by 10^(-6j/4095)", "high", "gram"),
+    "c5a": ("matmul 32768^3 precision=medium, N(0,1)", "medium", "matmul"),
+    "c5b": ("residual b - A x, A 32768^2 N(0,1) + 32768 I, x, b 32768x16", "high", "residual"),
+}
+
+
+def make_inputs(n, k, m):
+    """c2 (and --size): A (n x k) then B (k x m), i.i.d. N(0,1) from RandomState(0)."""
+    rng = np.random.RandomState(0)
+    A = rng.randn(n, k)
+    B = rng.randn(k, m)
+    return A, B
+
+
+def make_workload(name, size=8192):
+    """Host arrays of a configuration, drawn from RandomState(0):
+    c2  A then B, N(0,1)                                   (size^3)
+    c3  A's U(0,1), A's N(0,1), B's U(0,1), B's N(0,1); entry (U-0.5)*exp(10 N)
+    c4  A N(0,1) (65536 x 4096), then column j scaled by 10^(-6j/4095)
+    c5a A then B, N(0,1) (32768^2)
+    c5b A N(0,1) (32768^2) + 32768 I, then x, then b (32768 x 16 each)
+    Returns a dict with the operands and the shapes."""
+    rng = np.random.RandomState(0)
+    if name == "c2":
+        A, B = make_inputs(size, size, size)
+        return {"A": A, "B": B}
+    if name == "c3":
+        n, k, m = 4096, 8192, 4096
+        A = (rng.rand(n, k) - 0.5) * np.exp(10 * rng.randn(n, k))
+        B = (rng.rand(k, m) - 0.5) * np.exp(10 * rng.randn(k, m))
+        return {"A": A, "B": B}
+    if name == "c4":
+        n, k = 65536, 4096
+        A = rng.randn(n, k)
+        A *= 10.0 ** (-6.0 * np.arange(k) / 4095)
+        return {"A": A}
+    if name == "c5a":
+        n = 32768
+        A = rng.randn(n, n)
+        B = rng.randn(n, n)
+        return {"A": A, "B": B}
+    if name == "c5b":
+        n = 32768
+        A = rng.randn(n, n)
+        A[np.arange(n), np.arange(n)] += n
+        x = rng.randn(n, 16)
+        b = rng.randn(n, 16)
+        return {"A": A, "x": x, "b": b}
+    raise SystemExit(f"unknown workload {name!r}")
+
+
+# ---------------------------------------------------------------------------
+# Parity on the full-size inputs: blocks of the result against the oracle
+# ---------------------------------------------------------------------------
+
+def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import ozaki_oracle as O
-    rows = 32
+    return O
+
+
+def sample_blocks(n_rows, n_cols, rows=64, cols=256):
+    """The first and the last block of an n_rows x n_cols result: the last one
+    lies in the GEMM's last wave of tiles (the pair-split tiles, where a wave
+    is ragged)."""
+    r, c = min(rows, n_rows), min(cols, n_cols)
+    blocks = [(0, r, 0, c)]
+    last = (n_rows - r, n_rows, n_cols - c, n_cols)
+    if last != blocks[0]:
+        blocks.append(last)
+    return blocks
+
+
+def reference_blocks(kind, W, blocks, n_hi, n_lo):
+    """The reference's results on blocks of the identical input, and the exact
+    product there.  Rows of A and columns of B (lines of A for gram) are
+    extracted independently of each other, so the oracle on a block's rows and
+    columns gives exactly that block of the full-size reference result.
+    Returns three lists of blocks: the reference's fused result (FP32 2Sum, the
+    configuration's accumulation), its matmul_numpy(pipeline='ondevice')
+    result (FP64 sums), and the correctly rounded exact result."""
+    O = _oracle()
+    fused, numpy_, exact = [], [], []
+    for r0, r1, c0, c1 in blocks:
+        if kind == "matmul":
+            A, B = W["A"][r0:r1], W["B"][:, c0:c1]
+            fused.append(O.fused_ondevice(A, B, n_hi, n_lo)[2])
+            numpy_.append(O.ondevice_numpy(A, B, n_hi, n_lo))
+            exact.append(O.exact_product(A, B))
+        elif kind == "gram":
+            # G = (P + P^T)/2 with P = ozaki(A^T, A), rho from the row count
+            A = W["A"]
+            rho = O.compute_rho_f32(A.shape[0])
+            L, R = A[:, r0:r1].T, A[:, c0:c1]
+            p1 = O.fused_ondevice(L, R, n_hi, n_lo, rho)[2]
+            p2 = O.fused_ondevice(R.T, L.T, n_hi, n_lo, rho)[2]
+            fused.append((p1 + p2.T) * 0.5)
+            q1 = O.ondevice_numpy(L, R, n_hi, n_lo)
+            q2 = O.ondevice_numpy(R.T, L.T, n_hi, n_lo)
+            numpy_.append((q1 + q2.T) * 0.5)
+            exact.append(O.exact_product(L, R))
+        else:  # residual: b - A x, all columns of x
+            A, x, b = W["A"][r0:r1], W["x"], W["b"][r0:r1]
+            fused.append(b - O.fused_ondevice(A, x, n_hi, n_lo)[2])
+            numpy_.append(b - O.ondevice_numpy(A, x, n_hi, n_lo))
+            exact.append(b - O.exact_product(A, x))
+    return fused, numpy_, exact
+
+
+def parity_report(kind, W, ours_blocks, blocks, n_hi, n_lo):
+    """Normwise relative errors, against the exact product, of this build's
+    result and of the reference's on the same blocks of the same input; the
+    north star's bar is ours <= 1.5x the reference's."""
+    O = _oracle()
+    t0 = time.perf_counter()
+    fused, numpy_, exact = reference_blocks(kind, W, blocks, n_hi, n_lo)
+    cat = lambda xs: np.concatenate([x.ravel() for x in xs])
+    E = cat(exact)
+    e_ours = O.rel_err(cat(ours_blocks), E)
+    e_fused = O.rel_err(cat(fused), E)
+    e_numpy = O.rel_err(cat(numpy_), E)
+    finite = [e for e in (e_fused, e_numpy) if np.isfinite(e)]
+    e_ref = min(finite) if finite else float("inf")
+    floor = 32 * 2.0 ** -52
+    return {
+        "sample": "blocks [r0,r1)x[c0,c1) of the result: " + ", ".join(
+            f"[{r0},{r1})x[{c0},{c1})" for r0, r1, c0, c1 in blocks),
+        "exact": "correctly rounded FP64 result of the block (error-free split, math.fsum)",
+        "rel_err_ours": e_ours,
+        "rel_err_ref_fused": e_fused,
+        "rel_err_ref_numpy": e_numpy,
+        "ratio_to_ref": e_ours / e_ref if e_ref > 0 else None,
+        "within_1p5x_ref": bool(e_ours <= max(1.5 * e_ref, floor)),
+        "oracle_s": round(time.perf_counter() - t0, 1),
+    }
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline and the reference arm
+# ---------------------------------------------------------------------------
+
+def cpu_oracle_sample(A, B, n_hi, n_lo, budget_s=12.0, max_side=2048):
+    """Times the NumPy oracle (the reference's matmul_numpy(pipeline='ondevice')
+    restated) on the block C[0:s, 0:s] = A[0:s] @ B[:, 0:s] with all host
+    cores; rows of A and columns of B are extracted independently, so the
+    block is exactly that block of the full reference result and its work has
+    the full job's mix (GEMM-dominated).  The side s doubles from 256 until a
+    call takes budget_s / 3.  Returns (FP64-equiv TFLOP/s, s, seconds)."""
+    O = _oracle()
+    s = 256
+    k = A.shape[1]
     while True:
         t0 = time.perf_counter()
-        O.ondevice_numpy(A[:rows], B, n_hi, n_lo)
+        O.ondevice_numpy(A[:s], B[:, :s], n_hi, n_lo)
         dt = time.perf_counter() - t0
-        if dt >= budget_s / 3 or rows >= max_rows:
+        if dt >= budget_s / 3 or s >= max_side:
             break
-        rows *= 2
-    k, m = B.shape
-    return 2.0 * rows * k * m / dt / 1e12, rows, dt
+        s *= 2
+    return 2.0 * s * k * s / dt / 1e12, s, dt
 
 
 def reference_arm(args):
+    """--impl reference: the reference's own CPU implementation of the path,
+    the oracle port of matmul_numpy(pipeline='ondevice') (the reference is
+    Python and cannot travel to the GPU box; the port is pinned bit for bit to
+    the reference's own outputs).  Each step computes one bounded block of the
+    workload, C[0:s, 0:s] (s fixed in the first warm-up step), and the line
+    reports the measured rate on it; ms_per_step is that step's real time."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    O = _oracle()
     n = k = m = args.size
     n_hi, n_lo = PRESETS[args.precision]
     A, B = make_inputs(n, k, m)
-    vals = []
+    _, side, _ = cpu_oracle_sample(A, B, n_hi, n_lo, budget_s=9.0, max_side=2048)
+    times = []
     for i in range(args.warmup + args.steps):
-        v, rows, dt = cpu_oracle_sample(A, B, n_hi, n_lo, budget_s=6.0, max_rows=256)
+        t0 = time.perf_counter()
+        O.ondevice_numpy(A[:side], B[:, :side], n_hi, n_lo)
+        dt = time.perf_counter() - t0
         if i >= args.warmup:
-            vals.append((v, rows, dt))
-    v = statistics.median(x[0] for x in vals)
-    rows = vals[-1][1]
+            times.append(dt)
+    ms = statistics.mean(times) * 1e3
+    v = 2.0 * side * k * side / (ms * 1e-3) / 1e12
     cores = os.cpu_count()
     out = {
         "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 2.0 * n * k * m / (v * 1e12) * 1e3, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "impl": "reference",
-        "config": {"workload": f"matmul {n}x{k}x{m} precision={args.precision} "
-                               f"pipeline=ondevice (NumPy restatement of matmul_numpy)",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"matmul {n}x{k}x{m} pipeline=ondevice accumulation=fused "
+                               f"precision={args.precision}",
                    "N": n, "K": k, "M": m, "precision": args.precision},
         "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                         "sample": f"first {rows} rows of A x full B per step, "
-                                   f"extrapolated by FLOPs"},
+                         "sample": f"one step = the block C[0:{side}, 0:{side}] (A[0:{side}] x "
+                                   f"B[:, 0:{side}], K={k}) by the NumPy port of matmul_numpy"
+                                   f"(pipeline='ondevice'), OpenBLAS threads = cores; measured "
+                                   f"rate, not extrapolated"},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
+
+
+
+# ---------------------------------------------------------------------------
+# This build's arm
+# ---------------------------------------------------------------------------
+
+def _timed(call, steps, stream):
+    """Mean milliseconds of `steps` calls, CUDA events on the launching stream."""
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        call()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
 
 
 def ours(args):
@@ -289,333 +469,331 @@ def ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    name = args.workload
+    desc, precision, kind = WORKLOADS[name]
+    if name == "c2":
+        precision = args.precision
+        desc = f"matmul {args.size}^3 precision={precision}, N(0,1)"
+    if world > 1 and name != "c2":
+        raise SystemExit("--gpus > 1 runs the headline configuration (c2) only")
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
     lib = _lib.load()
     if args.l2_persist_mb > 0:
         _lib.check(lib.ozk_set_l2_persisting(int(args.l2_persist_mb) << 20, None))
-
-    n = k = m = args.size
-    n_hi, n_lo = PRESETS[args.precision]
+    n_hi, n_lo = PRESETS[precision]
     nS = n_hi + n_lo
-    A, B = make_inputs(n, k, m)
-    r0, r1 = rank * n // world, (rank + 1) * n // world
-    A_blk = np.ascontiguousarray(A[r0:r1])
-    nb = r1 - r0
-    Ad = torch.as_tensor(A_blk).to(dev)
-    Bd = torch.as_tensor(B).to(dev)
-    C = torch.empty((nb, m), dtype=torch.float64, device=dev)
-    rho = lib.ozk_compute_rho_f32(k)
-    # int8 slice codes where exact (rho >= 19: K > 4096), else BF16 slices
-    s8 = rho >= 19 and nb >= 256 and m >= 256 and not args.bf16
-    k_pad = (k + 127) // 128 * 128 if s8 else (k + 63) // 64 * 64
-    SA = torch.empty((nS, nb, k_pad), dtype=torch.int8 if s8 else torch.int16, device=dev)
-    SB = torch.empty((nS, m, k_pad), dtype=torch.int8 if s8 else torch.int16, device=dev)
-    fail = torch.zeros(1, dtype=torch.int32, device=dev)
-    eA = torch.empty((nS, nb), dtype=torch.int32, device=dev)
-    eB = torch.empty((nS, m), dtype=torch.int32, device=dev)
-    BT = torch.empty((m, k), dtype=torch.float64, device=dev)  # transposed-B scratch
-    GW = torch.empty(lib.ozk_slice_gemm_workspace_bytes(), dtype=torch.uint8, device=dev)
-    status = torch.zeros(1, dtype=torch.int32, device=dev)
-    pa = (ctypes.c_uint8 * 256)()
-    pb = (ctypes.c_uint8 * 256)()
-    # the pipeline's order for accumulation='fused' (order-independent sums)
-    npairs = lib.ozk_pair_schedule_snake(n_hi, n_lo, pa, pb, 256)
+    n_pairs = n_hi * n_hi + 2 * n_hi * n_lo
+
+    W = make_workload(name, args.size)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    if kind == "matmul":
+        A, B = W["A"], W["B"]
+        n, k = A.shape
+        m = B.shape[1]
+        r0, r1 = rank * n // world, (rank + 1) * n // world
+        A_blk = np.ascontiguousarray(A[r0:r1])
+        nb = r1 - r0
+        Ad = torch.as_tensor(A_blk).to(dev)
+        Bd = torch.as_tensor(B).to(dev)
+        C = torch.empty((nb, m), dtype=torch.float64, device=dev)
+        ws = torch.empty(lib.ozk_matmul_workspace_bytes(nb, k, m, n_hi, n_lo), dtype=torch.uint8,
+                         device=dev)
+        contraction = k
+        flops = 2.0 * n * k * m
 
-    ACC = _lib.OZK_ACC_FIXED  # accumulation='fused
+        def op():
+            _lib.check(lib.ozk_matmul_f64(Ad.data_ptr(), k, Bd.data_ptr(), m, C.data_ptr(), m, nb,
+                                          k, m, -1, n_hi, n_lo, _lib.OZK_ACC_FIXED, ws.data_ptr(),
+                                          ws.numel(), st.data_ptr(), sh))
+    elif kind == "gram":
+        A = W["A"]
+        n, k = A.shape
+        m = k
+        nb = k
+        Ad = torch.as_tensor(A).to(dev)
+        C = torch.empty((k, k), dtype=torch.float64, device=dev)
+        ws = torch.empty(lib.ozk_gram_workspace_bytes(n, k, n_hi, n_lo), dtype=torch.uint8,
+                         device=dev)
+        contraction = n
+        flops = 2.0 * n * k * k
 
-    def step(evs=None):
-        if evs:
-            evs[0].record(stream)
-        if s8:
-            _lib.check(lib.ozk_extract_rows_s8_f64(Ad.data_ptr(), k, nb, k, rho, n_hi, n_lo,
-                                                   SA.data_ptr(), k_pad, eA.data_ptr(),
-                                                   fail.data_ptr(), status.data_ptr(), sh))
-            _lib.check(lib.ozk_extract_cols_s8_f64(Bd.data_ptr(), m, k, m, rho, n_hi, n_lo,
-                                                   SB.data_ptr(), k_pad, eB.data_ptr(),
-                                                   BT.data_ptr(), BT.numel() * 8, fail.data_ptr(),
-                                                   status.data_ptr(), sh))
-        else:
-            _lib.check(lib.ozk_extract_rows_f64(Ad.data_ptr(), k, nb, k, rho, n_hi, n_lo,
-                                                SA.data_ptr(), k_pad, eA.data_ptr(),
-                                                status.data_ptr(), sh))
-            _lib.check(lib.ozk_extract_cols_f64(Bd.data_ptr(), m, k, m, rho, n_hi, n_lo,
-                                                SB.data_ptr(), k_pad, eB.data_ptr(),
-                                                BT.data_ptr(), BT.numel() * 8,
-                                                status.data_ptr(), sh))
-        if evs:
-            evs[1].record(stream)
-        if s8:
-            _lib.check(lib.ozk_slice_gemm_s8(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(),
-                                             eB.data_ptr(), nS, nb, m, k_pad, pa, pb, npairs, 0,
-                                             1.0, 0.0, None, 0, C.data_ptr(), m, GW.data_ptr(),
-                                             GW.numel(), rho, fail.data_ptr(), status.data_ptr(),
-                                             sh))
-        else:
-            _lib.check(lib.ozk_slice_gemm(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(),
-                                          eB.data_ptr(), nS, nb, m, k_pad, pa, pb, npairs,
-                                          ACC, 0, 1.0, 0.0, None, 0, C.data_ptr(), m,
-                                          None, GW.data_ptr(), GW.numel(), rho,
-                                          status.data_ptr(), sh))
-        if evs:
-            evs[2].record(stream)
+        def op():
+            _lib.check(lib.ozk_gram_f64(Ad.data_ptr(), k, C.data_ptr(), k, n, k, -1, n_hi, n_lo,
+                                        ws.data_ptr(), ws.numel(), st.data_ptr(), sh))
+    else:
+        A, x, b = W["A"], W["x"], W["b"]
+        n, k = A.shape
+        m = x.shape[1]
+        nb = n
+        Ad, Xd, bd = (torch.as_tensor(v).to(dev) for v in (A, x, b))
+        C = torch.empty((n, m), dtype=torch.float64, device=dev)
+        ws = torch.empty(lib.ozk_residual_workspace_bytes(n, k, m, n_hi, n_lo), dtype=torch.uint8,
+                         device=dev)
+        contraction = k
+        flops = 2.0 * n * k * m
+
+        def op():
+            _lib.check(lib.ozk_residual_f64(Ad.data_ptr(), k, Xd.data_ptr(), m, bd.data_ptr(), m,
+                                            C.data_ptr(), m, n, k, m, -1, n_hi, n_lo,
+                                            ws.data_ptr(), ws.numel(), st.data_ptr(), sh))
+    rho = lib.ozk_compute_rho_f32(contraction)
+    s8 = rho >= 19 and os.environ.get("OZK_S8", "1") != "0"
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
+    # ---- value: the C-ABI operator, inputs resident in HBM
     for _ in range(args.warmup):
-        step()
+        op()
     barrier()
-    assert status.item() == 0, f"device status {status.item()}"
-    assert fail.item() == 0, "a slice had no int8 code (inputs far outside the FP32 range)"
-
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    assert st.item() == 0, f"device status {st.item()}"
     clocks = Clocks(local)
     clocks.start()
     barrier()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
-    for i in range(args.steps):
-        step(ev[i])
+    for _ in range(args.steps):
+        op()
     t_end.record(stream)
     barrier()
+    op_ms = t_start.elapsed_time(t_end) / args.steps
+    assert st.item() == 0, f"device status {st.item()}"
+
+    # ---- the same kernels launched one by one, for the per-kernel split
+    breakdown, gemm_ms, extract_ms, kernel_launches = None, None, None, 0
+    if kind in ("matmul", "gram") and s8 and nb >= 256 and m >= 256:
+        k8 = (contraction + 127) // 128 * 128
+        fail = torch.zeros(1, dtype=torch.int32, device=dev)
+        pa = (ctypes.c_uint8 * 256)()
+        pb = (ctypes.c_uint8 * 256)()
+        npairs = lib.ozk_pair_schedule_snake(n_hi, n_lo, pa, pb, 256)
+        GW = torch.empty(lib.ozk_slice_gemm_workspace_bytes(), dtype=torch.uint8, device=dev)
+        if kind == "matmul":
+            SA = torch.empty((nS, nb, k8), dtype=torch.int8, device=dev)
+            SB = torch.empty((nS, m, k8), dtype=torch.int8, device=dev)
+            eA = torch.empty((nS, nb), dtype=torch.int32, device=dev)
+            eB = torch.empty((nS, m), dtype=torch.int32, device=dev)
+            BT = torch.empty((m, k), dtype=torch.float64, device=dev)
+
+            def extract():
+                _lib.check(lib.ozk_extract_rows_s8_f64(Ad.data_ptr(), k, nb, k, rho, n_hi, n_lo,
+                                                       SA.data_ptr(), k8, eA.data_ptr(),
+                                                       fail.data_ptr(), st.data_ptr(), sh))
+                _lib.check(lib.ozk_extract_cols_s8_f64(Bd.data_ptr(), m, k, m, rho, n_hi, n_lo,
+                                                       SB.data_ptr(), k8, eB.data_ptr(),
+                                                       BT.data_ptr(), BT.numel() * 8,
+                                                       fail.data_ptr(), st.data_ptr(), sh))
+
+            def gemm():
+                _lib.check(lib.ozk_slice_gemm_s8(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(),
+                                                 eB.data_ptr(), nS, nb, m, k8, pa, pb, npairs, 0,
+                                                 1.0, 0.0, None, 0, C.data_ptr(), m, GW.data_ptr(),
+                                                 GW.numel(), rho, fail.data_ptr(), st.data_ptr(),
+                                                 sh))
+            per_step = 4
+        else:
+            SA = torch.empty((nS, k, k8), dtype=torch.int8, device=dev)
+            eA = torch.empty((nS, k), dtype=torch.int32, device=dev)
+            BT = torch.empty((k, n), dtype=torch.float64, device=dev)
+
+            def extract():
+                _lib.check(lib.ozk_extract_cols_s8_f64(Ad.data_ptr(), k, n, k, rho, n_hi, n_lo,
+                                                       SA.data_ptr(), k8, eA.data_ptr(),
+                                                       BT.data_ptr(), BT.numel() * 8,
+                                                       fail.data_ptr(), st.data_ptr(), sh))
+
+            def gemm():
+                _lib.check(lib.ozk_slice_gemm_s8(SA.data_ptr(), eA.data_ptr(), nS, SA.data_ptr(),
+                                                 eA.data_ptr(), nS, k, k, k8, pa, pb, npairs, 1,
+                                                 1.0, 0.0, None, 0, C.data_ptr(), k, GW.data_ptr(),
+                                                 GW.numel(), rho, fail.data_ptr(), st.data_ptr(),
+                                                 sh))
+            per_step = 3
+        for _ in range(args.warmup):
+            extract()
+            gemm()
+        barrier()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        barrier()
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            extract()
+            ev[i][1].record(stream)
+            gemm()
+            ev[i][2].record(stream)
+        barrier()
+        assert fail.item() == 0 and st.item() == 0
+        extract_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+        gemm_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+        kernel_launches = per_step * args.steps
+        del SA, eA, BT
     clk = clocks.stop()
-    total_ms = t_start.elapsed_time(t_end)
-    gemm_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
-    extract_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
     if world > 1:
-        t = torch.tensor([total_ms, gemm_ms, extract_ms], dtype=torch.float64, device=dev)
+        t = torch.tensor([op_ms, gemm_ms or 0.0, extract_ms or 0.0], dtype=torch.float64,
+                         device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, gemm_ms, extract_ms = t.tolist()
-    gemm_waits = None
-    if os.environ.get("OZK_GEMM_STATS") == "1":
-        w = (ctypes.c_ulonglong * 8)()
-        n_ctas = lib.ozk_gemm_stats(w)
-        if n_ctas > 0 and w[3]:
-            gemm_waits = {"mma_wait_accumulator": w[0] / w[3], "mma_wait_loads": w[1] / w[3],
-                          "producer_wait_free_stage_cycles_per_cta": w[2] / n_ctas,
-                          "mma_total_cycles_per_cta": w[3] / n_ctas,
-                          "epilogue_wait_cycles_per_pair": w[4] / max(w[6], 1),
-                          "epilogue_busy_cycles_per_pair": w[5] / max(w[6], 1),
-                          "mma_wait_loads_pair_head": w[7] / w[3]}
-    ms_step = total_ms / args.steps
-    flops_fp64eq = 2.0 * n * k * m
-    value = flops_fp64eq / (ms_step * 1e-3) / 1e12
+        op_ms, g, e = t.tolist()
+        gemm_ms, extract_ms = (g or None), (e or None)
+    value = flops / (op_ms * 1e-3) / 1e12
 
-    # accuracy of this rank's block against native FP64 (cuBLAS DGEMM)
-    R = torch.matmul(Ad, Bd)
-    rel_err = float(torch.linalg.norm(C - R) / torch.linalg.norm(R))
-    # native FP64 DGEMM throughput on the same block, for comparison
-    for _ in range(2):
-        torch.matmul(Ad, Bd, out=R)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(3):
-        torch.matmul(Ad, Bd, out=R)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    dgemm_tflops_rank = 2.0 * nb * k * m / (e0.elapsed_time(e1) / 3 * 1e-3) / 1e12
-    del R
-
-    # end to end through the public API from pinned host memory
-    pinA = torch.empty(A_blk.shape, dtype=torch.float64, pin_memory=True)
-    pinA.numpy()[...] = A_blk
-    pinB = torch.empty(B.shape, dtype=torch.float64, pin_memory=True)
-    pinB.numpy()[...] = B
-    hA, hB = pinA.numpy(), pinB.numpy()
-    if world == 1:
-        e2e_call = lambda: oz.matmul(hA, hB, pipeline="ondevice", precision=args.precision)
+    # ---- parity on the full-size input: blocks of this rank's result
+    blocks = sample_blocks(nb, m)
+    Ch = [C[r0_:r1_, c0_:c1_].cpu().numpy() for r0_, r1_, c0_, c1_ in blocks]
+    if kind == "matmul":
+        Wr = {"A": W["A"][r0:r1], "B": W["B"]}
     else:
-        # each rank uploads its rows of A and 1/P of B; B is all-gathered over NCCL
-        from ozaki_jax_b200.distributed import matmul_rowsharded_host
-        e2e_call = lambda: matmul_rowsharded_host(hA, hB, precision=args.precision)
-    # two warm-up calls: the result of one call is still alive while the next
-    # runs, so torch's pinned-host pool needs two output buffers
-    Ch = e2e_call()
-    Ch = e2e_call()
-    barrier()
-    e2e_steps = max(1, min(args.steps, 3))
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        Ch = e2e_call()
-    e1.record(stream)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = t.item()
-    assert Ch.shape == (nb, m)
+        Wr = W
+    parity = parity_report(kind, Wr, Ch, blocks, n_hi, n_lo) if rank == 0 else None
+
+    # ---- native FP64 (cuBLAS DGEMM) on the same operands, for comparison
+    if kind == "matmul":
+        ref = lambda: torch.matmul(Ad, Bd)
+    elif kind == "gram":
+        ref = lambda: torch.matmul(Ad.T, Ad)
+    else:
+        ref = lambda: bd - torch.matmul(Ad, Xd)
+    R = ref()
+    rel_err_dgemm = float(torch.linalg.norm(C - R) / torch.linalg.norm(R))
+    del R
+    dgemm_ms = _timed(lambda: ref(), 3, stream)
+    dgemm_tflops = flops / (dgemm_ms * 1e-3) / 1e12  # every rank runs its share at once
+
+    # ---- end to end through the public API, host arrays in and out
+    def e2e_case(pinned):
+        import torch as T
+        host = {}
+        srcs = {"matmul": ("A", "B"), "gram": ("A",), "residual": ("A", "x", "b")}[kind]
+        for key in srcs:
+            v = np.ascontiguousarray(A_blk if (kind == "matmul" and key == "A") else W[key])
+            if pinned:
+                p = T.empty(v.shape, dtype=T.float64, pin_memory=True)
+                p.numpy()[...] = v
+                v = p.numpy()
+            host[key] = v
+        if kind == "matmul" and world == 1:
+            return lambda: oz.matmul(host["A"], host["B"], pipeline="ondevice", precision=precision)
+        if kind == "matmul":
+            from ozaki_jax_b200.distributed import matmul_rowsharded_host
+            return lambda: matmul_rowsharded_host(host["A"], host["B"], precision=precision)
+        if kind == "gram":
+            return lambda: oz.gram(host["A"], precision=precision, mode="ozaki")
+        return lambda: oz.residual(host["A"], host["x"], host["b"], precision=precision,
+                                   mode="ozaki")
+
+    def e2e_time(call):
+        # two warm-up calls: one result is still alive while the next runs
+        out = call()
+        out = call()
+        barrier()
+        steps = max(1, min(args.steps, 3))
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            out = call()
+        t1.record(stream)
+        barrier()
+        ms = t0.elapsed_time(t1) / steps
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        assert out.shape == (nb, m)
+        return ms
+    e2e_ms = e2e_time(e2e_case(pinned=False))
+    e2e_pinned_ms = e2e_time(e2e_case(pinned=True))
 
     l2_prev = ctypes.c_size_t(0)
     _lib.check(lib.ozk_set_l2_persisting(ctypes.c_size_t(-1).value, ctypes.byref(l2_prev)))
-    if rank == 0:
-        bf16_peak, hbm_peak, src = peaks()
-        gemm_tflops = npairs * 2.0 * nb * k * m / (gemm_ms * 1e-3) / 1e12
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    bf16_peak, hbm_peak, src = peaks()
+    op_launches = {"matmul": 7, "gram": 5, "residual": 7}[kind] if s8 else 3
+    out = {
+        "metric": METRIC if name == "c2" else (
+            "FP64-equiv TFLOP/s (2NK^2/t)" if kind == "gram" else "FP64-equiv TFLOP/s (2MNK/t)"),
+        "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": op_ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (np.random.RandomState(0), BASELINE's recipe)",
+        "config": {"workload": f"{name}: {desc} ({n_pairs} slice GEMMs), "
+                               f"accumulation={'bf16_interleaved' if kind != 'matmul' else 'fused'}",
+                   "N": n, "K": k, "M": m, "precision": precision, "rho": rho,
+                   "slices": "int8 codes" if s8 else "bf16",
+                   "parallelism": f"row-blocks x{world}" if kind == "matmul" else "1 GPU",
+                   "timed": "ozk_matmul_f64 (the C-ABI operator, all its launches)"
+                            if kind == "matmul" else f"ozk_{kind}_f64 (the C-ABI operator)",
+                   "l2": "inputs larger than L2 (126 MB), no flush",
+                   "l2_persisting_mb_after": round(l2_prev.value / 2**20, 1)},
+        "parity": parity,
+        "rel_err_vs_cublas_dgemm": rel_err_dgemm,
+        "dgemm_fp64_tflops": dgemm_tflops,
+        "breakdown_ms": {"operator": op_ms, "extract": extract_ms, "slice_gemm": gemm_ms,
+                         "note": "extract / slice_gemm: the operator's kernels launched one by one "
+                                 "in a second timed loop"},
+        "clocks": clk,
+        "gpu_launches": op_launches * args.steps + kernel_launches,
+    }
+    if kind in ("matmul", "gram") and gemm_ms:
+        tensor = n_pairs * flops / world
+        if kind == "gram":
+            tiles = (k // 256) * (k // 256 + 1) / 2 / (k // 256) ** 2
+            tensor *= tiles
         mma_peak, mma_unit, peak_src, peak_extra = tensor_peak(s8, dev)
-        ext_bytes = (8.0 * (nb * k + k * m) + (1.0 if s8 else 2.0) * nS * (nb + m) * k_pad
-                     + 4.0 * nS * (nb + m))
-        cpu_v, cpu_rows, cpu_dt = cpu_oracle_sample(A, B, n_hi, n_lo)
-        out = {
-            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
-            "data": "synthetic",
-            "config": {"workload": f"matmul {n}x{k}x{m} pipeline=ondevice accumulation=fused "
-                                   f"precision={args.precision} ({npairs} slice GEMMs)",
-                       "N": n, "K": k, "M": m, "precision": args.precision,
-                       "slices": "int8 codes" if s8 else "bf16",
-                       "parallelism": f"row-blocks x{world}", "l2": "inputs 1 GiB > L2, no flush",
-                       "l2_persisting_mb": round(l2_prev.value / 2**20, 1)},
-            "rel_err": rel_err,
-            "dgemm_fp64_tflops": dgemm_tflops_rank * world,
-            "breakdown_ms": {"extract": extract_ms, "slice_gemm": gemm_ms},
-            "gemm_wait_fractions": gemm_waits,
-            "roofline": {"bound": "tensor", "kernel": "k_slice_gemm",
-                         "mma": "int8 x int8 -> int32" if s8 else "bf16 x bf16 -> fp32",
-                         "achieved": gemm_tflops, "peak": mma_peak, "unit": mma_unit,
-                         "frac": gemm_tflops / mma_peak, "peak_source": peak_src, **peak_extra,
-                         "frac_of_int8_library_gemm": (gemm_tflops / peak_extra["int8_library_gemm"]
-                                                       if peak_extra.get("int8_library_gemm")
-                                                       else None),
-                         "traffic": GEMM_TRAFFIC_BYTES.get(
-                             (n, args.precision, "int8" if s8 else "bf16")) if world == 1 else None,
-                         "traffic_unit": "bytes per launch (ncu dram__bytes_read+write)",
-                         "extract": {"bound": "hbm", "achieved_gbs": ext_bytes / (extract_ms * 1e-3) / 1e9,
-                                     "peak_gbs": hbm_peak,
-                                     "frac": ext_bytes / (extract_ms * 1e-3) / 1e9 / hbm_peak}},
-            "cpu_baseline": {"value": cpu_v, "unit": "TFLOP/s", "cores": os.cpu_count(),
-                             "kind": "port",
-                             "sample": f"first {cpu_rows} rows of A x full B ({cpu_dt:.1f} s), "
-                                       f"NumPy oracle, OpenBLAS threads = cores"},
-            # copies of the whole job (all ranks): A and C once, B once in total
-            # (world == 1) or in per-rank shares padded to ceil(K/P) rows
-            "e2e": {"value": flops_fp64eq / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": int(8 * (n * k + (k * m if world == 1 else
-                                                            world * ((k + world - 1) // world) * m))),
-                    "d2h_bytes_per_step": int(8 * n * m)},
-            "clocks": clk,
-            "gpu_launches": 4 * args.steps,
-        }
-        print(json.dumps(out), flush=True)
+        ach = tensor / (gemm_ms * 1e-3) / 1e12
+        ext_bytes = (8.0 * (nb * k + k * m) + 1.0 * nS * (nb + m) * k8 + 4.0 * nS * (nb + m)
+                     if kind == "matmul" else 8.0 * n * k + nS * k * k8 + 4.0 * nS * k)
+        out["roofline"] = {
+            "bound": "tensor", "kernel": "k_slice_gemm", "mma": "int8 x int8 -> int32",
+            "achieved": ach, "peak": mma_peak, "unit": mma_unit, "frac": ach / mma_peak,
+            "peak_source": peak_src, **peak_extra,
+            "frac_of_int8_library_gemm": (ach / peak_extra["int8_library_gemm"]
+                                          if peak_extra.get("int8_library_gemm") else None),
+            "traffic": GEMM_TRAFFIC_BYTES.get((n, precision, "int8")) if world == 1 else None,
+            "traffic_unit": "bytes per launch (ncu dram__bytes_read+write)",
+            "extract": {"bound": "hbm", "achieved_gbs": ext_bytes / (extract_ms * 1e-3) / 1e9,
+                        "peak_gbs": hbm_peak,
+                        "frac": ext_bytes / (extract_ms * 1e-3) / 1e9 / hbm_peak}}
+    elif kind == "residual":
+        a_bytes = 8.0 * n * k
+        out["roofline"] = {"bound": "hbm", "kernel": "the residual operator",
+                           "achieved": a_bytes / (op_ms * 1e-3) / 1e9, "peak": hbm_peak,
+                           "unit": "GB/s", "frac": a_bytes / (op_ms * 1e-3) / 1e9 / hbm_peak,
+                           "peak_source": src, "traffic": None,
+                           "note": "algorithmic bytes = one read of A"}
+    # copies of the whole job (all ranks): A and C once, B once in total
+    # (world == 1) or in per-rank shares padded to ceil(K/P) rows
+    if kind == "matmul":
+        h2d = 8 * (n * k + (k * m if world == 1 else world * ((k + world - 1) // world) * m))
+        d2h = 8 * n * m
+    elif kind == "gram":
+        h2d, d2h = 8 * n * k, 8 * k * k
+    else:
+        h2d, d2h = 8 * (n * k + 2 * n * m), 8 * n * m
+    out["e2e"] = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                  "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                  "host_memory": "pageable NumPy arrays (what a drop-in caller passes)",
+                  "pinned_value": flops / (e2e_pinned_ms * 1e-3) / 1e12}
+    if name == "c2" or args.cpu_baseline:
+        if kind == "matmul":
+            cpu_v, side, cpu_dt = cpu_oracle_sample(W["A"], W["B"], n_hi, n_lo)
+            out["cpu_baseline"] = {
+                "value": cpu_v, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+                "sample": f"block C[0:{side}, 0:{side}] ({cpu_dt:.1f} s) by the NumPy port of "
+                          f"matmul_numpy(pipeline='ondevice'), OpenBLAS threads = cores"}
+    print(json.dumps(out), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
-
-WORKLOADS = {
-    # name: (description, precision)
-    "c3": ("matmul 4096x8192x4096 precision=max, (U(0,1)-0.5)*exp(10*N(0,1)) entries", "max"),
-    "c4": ("gram A^T A, A 65536x4096 N(0,1), column j scaled by 10^(-6j/4095)", "high"),
-    "c5a": ("matmul 32768^3 precision=medium, N(0,1)", "medium"),
-    "c5b": ("residual b - A x, A 32768^2 N(0,1) + 32768 I, x, b 32768x16", "high"),
-}
-
-
-def other_workload(args):
-    """The other benchmark configurations (c3 'max' on wide-range entries, c4
-    gram, c5a 'medium' 32768^3, c5b residual) on one GPU, through the C entry
-    points on device arrays (inputs drawn on the device from a seeded torch
-    generator with each configuration's distribution).  Prints one JSON line."""
-    import torch
-    from ozaki_jax_b200 import _lib
-
-    lib = _lib.load()
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    desc, precision = WORKLOADS[args.workload]
-    n_hi, n_lo = PRESETS[precision]
-    n_pairs = n_hi * n_hi + 2 * n_hi * n_lo
-    g = torch.Generator(device=dev)
-    g.manual_seed(0)
-    randn = lambda *shape: torch.randn(*shape, generator=g, device=dev, dtype=torch.float64)
-    st = torch.zeros(1, dtype=torch.int32, device=dev)
-    sh = torch.cuda.current_stream(dev).cuda_stream
-    w = args.workload
-    if w in ("c3", "c5a"):
-        n, k, m = (4096, 8192, 4096) if w == "c3" else (32768, 32768, 32768)
-        if w == "c3":
-            A = (torch.rand(n, k, generator=g, device=dev, dtype=torch.float64) - 0.5) * torch.exp(10 * randn(n, k))
-            B = (torch.rand(k, m, generator=g, device=dev, dtype=torch.float64) - 0.5) * torch.exp(10 * randn(k, m))
-        else:
-            A, B = randn(n, k), randn(k, m)
-        C = torch.empty((n, m), dtype=torch.float64, device=dev)
-        ws = torch.empty(lib.ozk_matmul_workspace_bytes(n, k, m, n_hi, n_lo), dtype=torch.uint8, device=dev)
-        call = lambda: _lib.check(lib.ozk_matmul_f64(
-            A.data_ptr(), k, B.data_ptr(), m, C.data_ptr(), m, n, k, m, -1, n_hi, n_lo,
-            _lib.OZK_ACC_FIXED, ws.data_ptr(), ws.numel(), st.data_ptr(), sh))
-        flops, contraction, ref = 2.0 * n * k * m, k, (lambda: torch.matmul(A, B))
-    elif w == "c4":
-        n, k = 65536, 4096
-        A = randn(n, k) * torch.pow(10.0, -6.0 * torch.arange(k, device=dev, dtype=torch.float64) / 4095)
-        C = torch.empty((k, k), dtype=torch.float64, device=dev)
-        ws = torch.empty(lib.ozk_gram_workspace_bytes(n, k, n_hi, n_lo), dtype=torch.uint8, device=dev)
-        call = lambda: _lib.check(lib.ozk_gram_f64(
-            A.data_ptr(), k, C.data_ptr(), k, n, k, -1, n_hi, n_lo, ws.data_ptr(), ws.numel(),
-            st.data_ptr(), sh))
-        flops, contraction, ref = 2.0 * n * k * k, n, (lambda: torch.matmul(A.T, A))
-    else:
-        n, m = 32768, 16
-        k = n
-        A = randn(n, n)
-        A.diagonal().add_(float(n))
-        X, Bv = randn(n, m), randn(n, m)
-        C = torch.empty((n, m), dtype=torch.float64, device=dev)
-        ws = torch.empty(lib.ozk_residual_workspace_bytes(n, n, m, n_hi, n_lo), dtype=torch.uint8, device=dev)
-        call = lambda: _lib.check(lib.ozk_residual_f64(
-            A.data_ptr(), n, X.data_ptr(), m, Bv.data_ptr(), m, C.data_ptr(), m, n, n, m, -1,
-            n_hi, n_lo, ws.data_ptr(), ws.numel(), st.data_ptr(), sh))
-        flops, contraction, ref = 2.0 * n * n * m, n, (lambda: Bv - torch.matmul(A, X))
-    for _ in range(args.warmup):
-        call()
-    torch.cuda.synchronize(dev)
-    assert st.item() == 0, f"device status {st.item()}"
-    clocks = Clocks(0)
-    clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        call()
-    e1.record()
-    torch.cuda.synchronize(dev)
-    clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / args.steps
-    R = ref()
-    rel_err = float(torch.linalg.norm(C - R) / torch.linalg.norm(R))
-    del R
-    rho = lib.ozk_compute_rho_f32(contraction)
-    s8 = rho >= 19
-    bf16_peak, hbm_peak, src = peaks()
-    out = {"metric": "FP64-equiv TFLOP/s (2MNK/t)" if w != "c4" else "FP64-equiv TFLOP/s (2NK^2/t)",
-           "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-           "higher_is_better": True, "dtype": "f64", "data": "synthetic (torch CUDA generator, seed 0)",
-           "config": {"workload": f"{w}: {desc}", "precision": precision,
-                      "slices": "int8 codes" if s8 else "bf16", "rho": rho},
-           "rel_err_vs_cublas_dgemm": rel_err, "clocks": clk}
-    if w == "c5b":
-        a_bytes = 8.0 * n * n
-        out["roofline"] = {"bound": "hbm", "achieved": a_bytes / (ms * 1e-3) / 1e9,
-                           "peak": hbm_peak, "unit": "GB/s", "frac": a_bytes / (ms * 1e-3) / 1e9 / hbm_peak,
-                           "note": "algorithmic bytes = one read of A", "peak_source": src}
-    else:
-        tensor = n_pairs * flops
-        if w == "c4":
-            # only the tiles on or above the diagonal are computed
-            tiles = (k // 256) * (k // 256 + 1) / 2 / (k // 256) ** 2
-            tensor *= tiles
-        peak, unit, psrc, extra = tensor_peak(s8, dev)
-        ach = tensor / (ms * 1e-3) / 1e12
-        out["roofline"] = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": unit,
-                           "frac": ach / peak, "peak_source": psrc, **extra}
-        if extra.get("int8_library_gemm"):
-            out["roofline"]["frac_of_int8_library_gemm"] = ach / extra["int8_library_gemm"]
-    print(json.dumps(out), flush=True)
 
 
 def kernel_case(spec, steps):
@@ -691,16 +869,16 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--size", type=int, default=8192)
-    ap.add_argument("--precision", choices=sorted(PRESETS), default="high")
-    ap.add_argument("--bf16", action="store_true",
-                    help="BF16 slices even where int8 codes are exact (comparison)")
+    ap.add_argument("--size", type=int, default=8192, help="c2 only: N = K = M")
+    ap.add_argument("--precision", choices=sorted(PRESETS), default="high", help="c2 only")
     ap.add_argument("--l2-persist-mb", type=int, default=0,
                     help="persisting-L2 set-aside for the GEMM's running sums in MB "
                          "(0: the library's own choice)")
-    ap.add_argument("--workload", choices=["c2"] + sorted(WORKLOADS), default="c2",
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2",
                     help="c2 (default): the headline 8192^3 line; others: the remaining "
                          "benchmark configurations on one GPU")
+    ap.add_argument("--cpu-baseline", action="store_true",
+                    help="also time the CPU oracle for a workload other than c2")
     ap.add_argument("--case", default=None,
                     help="profiling aid, not a bench line: one small single-kernel case, "
                          "extract:ROWSxK, cols:KxCOLS or residual:ROWSxK (--steps calls "
@@ -708,8 +886,6 @@ def main():
     args = ap.parse_args()
     if args.case:
         kernel_case(args.case, args.steps)
-    elif args.workload != "c2" and args.impl == "ours":
-        other_workload(args)
     elif args.impl == "reference":
         reference_arm(args)
     else:

@@ -239,12 +239,20 @@ int ozk_matmul_f64_hostbuf(const double* A, int64_t lda, const double* B, int64_
  * such as JAX/XLA reserving most of it for its own allocator, or a plugin
  * callback its host forbids from allocating): the slice workspace comes from a
  * fixed device array of OZK_NOALLOC_SCRATCH_BYTES compiled into the library,
- * held by every GPU that loads it until exit.  Requests whose workspace
- * (ozk_matmul_workspace_bytes) exceeds it return OZK_ERR_WORKSPACE;
- * 1024 x 1024 x 1024 at (4, 1) fits.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress) and should come before any
+ * held by every GPU that loads it until exit.  The bound is the slices-only
+ * workspace (not ozk_matmul_workspace_bytes, which adds the GEMM state scratch
+ * of about 38 MB): with nS = n_hi + n_lo and k_pad = K rounded up to 64,
+ *   align256(2 nS N k_pad) + align256(2 nS M k_pad) + align256(4 nS N)
+ *   + align256(4 nS M) + align256(8 K M) + 256 <= OZK_NOALLOC_SCRATCH_BYTES,
+ * else OZK_ERR_WORKSPACE; 1024 x 1024 x 1024 at (4, 1) fits.  Without the
+ * state scratch the slice GEMM runs its 128-wide BF16 tiles (running sums in
+ * TMEM; at most 16 columns use the int8 skinny kernel); the sums are exact,
+ * so C is bit-identical to ozk_matmul_f64 with OZK_ACC_FIXED.  Each call looks
+ * up the array's address in the current context (cudaGetSymbolAddress); the
+ * first call in a context also loads the module and should come before any
  * stream capture.  All calls share the array; calls that overlap on the GPU
- * race on it and must be serialised by the caller.  No cudaMalloc/cudaFree. */
+ * race on it and must be serialised by the caller.  No cudaMalloc/cudaFree
+ * (OZK_GEMM_STATS diagnostics record nothing for these calls). */
 #define OZK_NOALLOC_SCRATCH_BYTES (32 * 1024 * 1024)
 int ozk_matmul_f64_noalloc(const double* A, int64_t lda, const double* B, int64_t ldb, double* C,
                            int64_t ldc, int64_t N, int64_t K, int64_t M, int n_hi, int n_lo,
@@ -292,7 +300,8 @@ int ozk_last_error_detail(char* buf, size_t len);
  * accumulator, 5: epilogue cycles processing, 6: epilogue pairs, 7: the part
  * of 1 spent in the first pipeline-depth k-blocks of each pair}
  * (epilogue figures from one warp per CTA); returns the CTA count
- * (synchronises the device). */
+ * (synchronises the device).  The counters are allocated on the first
+ * recorded launch; launches without the GEMM state scratch record none. */
 int ozk_gemm_stats(unsigned long long* out8);
 /* Failure-path self-test (no counterpart in the reference): one CTA waits on an
  * mbarrier nothing arrives at, through the bounded wait all kernels use; after
@@ -303,14 +312,17 @@ int ozk_selftest_timeout(int budget_ms, int32_t* status_dev, int32_t* ok_dev, vo
  * reference).  The 256-wide GEMM tiles keep per-CTA running sums in a global
  * scratch (ozk_slice_gemm_workspace_bytes, about 38 MB) that it re-reads every
  * pair, and it marks those accesses evict_last.  That priority takes effect
- * only inside the context's persisting-L2 set-aside.  The library raises the
- * set-aside to hold the sums on its first 256-wide GEMM launch on a device
- * (never lowering it; OZK_L2_PERSIST=0 in the environment leaves it alone,
- * OZK_L2_PERSIST=<MB> asks for that size).  This call sets it explicitly:
- * `bytes` (clamped to the device maximum; 0 turns it off; (size_t)-1 only
- * queries), the value in force before goes to *previous (may be NULL).  The
- * limit belongs to this process's CUDA context and ends with it; lines not
- * marked persisting may use the set-aside while no persisting data holds it. */
+ * only inside the context's persisting-L2 set-aside, so around each 256-wide
+ * launch the library raises the set-aside to hold the sums and puts the
+ * previous limit back as soon as the kernel is enqueued: the caller's other
+ * kernels keep their own setting.  (OZK_L2_PERSIST=0 in the environment
+ * leaves the limit alone, OZK_L2_PERSIST=<MB> asks for that size, and
+ * OZK_L2_PERSIST=sticky raises it once per device and keeps it.)  This call
+ * sets the limit explicitly: `bytes` (clamped to the device maximum; 0 turns
+ * it off; (size_t)-1 only queries), the value in force before goes to
+ * *previous (may be NULL).  The limit belongs to this process's CUDA context
+ * and ends with it; lines not marked persisting may use the set-aside while no
+ * persisting data holds it. */
 int ozk_set_l2_persisting(size_t bytes, size_t* previous);
 /* Library version string. */
 const char* ozk_version(void);

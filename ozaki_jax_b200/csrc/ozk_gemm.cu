@@ -904,7 +904,9 @@ static int launch_bn(const CUtensorMap& ma, const CUtensorMap& mb, const PairLis
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   GemmArgs gl = ga;
-  if (stats_enabled()) {
+  // Diagnostics allocate their counters on first use; calls without the state
+  // scratch (the allocation-free entry point among them) record none.
+  if (stats_enabled() && ga.state) {
     if (!g_stats_dev[dev]) cudaMalloc(&g_stats_dev[dev], 8 * 1024 * sizeof(unsigned long long));
     cudaMemsetAsync(g_stats_dev[dev], 0, 8 * 1024 * sizeof(unsigned long long), stream);
     gl.stats = g_stats_dev[dev];
@@ -947,34 +949,48 @@ static int pace_slack() {
 }
 
 // The running sums are marked evict_last; that priority applies inside the
-// context's persisting-L2 set-aside.  On the first 256-wide launch on a device
-// the set-aside is raised to hold them (never lowered; OZK_L2_PERSIST=0 leaves
-// it alone, OZK_L2_PERSIST=<MB> asks for that size).  Measured on B200 at
-// 8192^3 with int8 slices: DRAM writes of the GEMM drop from 11.7 GB to 0.5 GB.
-static void ensure_l2_persisting(int dev, cudaStream_t stream) {
-  static int done[64] = {0};
-  if (dev < 0 || dev >= 64 || done[dev]) return;
-  done[dev] = 1;
-  const char* env = getenv("OZK_L2_PERSIST");
-  size_t want = gemm_state_sums_bytes(dev) + (8u << 20);
-  if (env) {
-    const long mb = atol(env);
-    if (mb <= 0) return;
-    want = (size_t)mb << 20;
+// context's persisting-L2 set-aside.  Measured on B200 at 8192^3 with int8
+// slices: with a set-aside that holds them, DRAM writes of the GEMM drop from
+// 11.7 GB to 0.5 GB.  The set-aside is a limit of the whole CUDA context, so
+// by default it is raised only around the library's own launch: the limit in
+// force before is put back as soon as the kernel is enqueued, and the caller's
+// other kernels see their own setting.  OZK_L2_PERSIST=0 leaves the limit
+// alone, OZK_L2_PERSIST=<MB> asks for that size (still restored), and
+// OZK_L2_PERSIST=sticky raises it once per device and keeps it (the behaviour
+// of earlier versions, kept for comparisons).
+struct L2Scope {
+  bool restore = false;
+  size_t prev = 0;
+  void raise(int dev, cudaStream_t stream, size_t sums_bytes) {
+    static int sticky_done[64] = {0};
+    const char* env = getenv("OZK_L2_PERSIST");
+    const bool sticky = env && strcmp(env, "sticky") == 0;
+    size_t want = sums_bytes + (8u << 20);
+    if (env && !sticky) {
+      const long mb = atol(env);
+      if (mb <= 0) return;
+      want = (size_t)mb << 20;
+    }
+    if (sticky && (dev < 0 || dev >= 64 || sticky_done[dev])) return;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
+      return;  // a limit change is not a capturable operation
+    size_t cur = 0;
+    int mx = 0;
+    if (cudaDeviceGetLimit(&cur, cudaLimitPersistingL2CacheSize) != cudaSuccess ||
+        cudaDeviceGetAttribute(&mx, cudaDevAttrMaxPersistingL2CacheSize, dev) != cudaSuccess)
+      return;
+    if (want > (size_t)mx) want = (size_t)mx;
+    if (sticky) sticky_done[dev] = 1;
+    if (cur >= want) return;
+    if (cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, want) != cudaSuccess) return;
+    restore = !sticky;
+    prev = cur;
   }
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
-    done[dev] = 0;  // try again on a later, uncaptured launch
-    return;
+  ~L2Scope() {
+    if (restore) cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, prev);
   }
-  size_t cur = 0;
-  int mx = 0;
-  if (cudaDeviceGetLimit(&cur, cudaLimitPersistingL2CacheSize) != cudaSuccess ||
-      cudaDeviceGetAttribute(&mx, cudaDevAttrMaxPersistingL2CacheSize, dev) != cudaSuccess)
-    return;
-  if (want > (size_t)mx) want = (size_t)mx;
-  if (cur < want) cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, want);
-}
+};
 
 int launch_slice_gemm(const uint16_t* SA, const int32_t* eA, int nA, const uint16_t* SB,
                       const int32_t* eB, int nB, int64_t N, int64_t M, int64_t k_pad,
@@ -1004,6 +1020,7 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
                          size_t state_bytes, int rho, int32_t* status, bool s8,
                          const int32_t* gate, int gate_want, cudaStream_t stream) {
   if (N == 0 || M == 0) return OZK_OK;
+  L2Scope l2;  // a raised persisting-L2 limit is put back when this returns
   if (n_pairs < 1 || n_pairs > OZK_MAX_PAIRS) return set_error(OZK_ERR_ARG, "n_pairs out of range");
   if (k_pad <= 0 || k_pad % OZK_KB) return set_error(OZK_ERR_ARG, "k_pad must be a positive multiple of 64");
   if (s8 && !slice_gemm_s8_eligible(N, M, k_pad, mode, rho, state_bytes))
@@ -1082,7 +1099,7 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
   ga.gate = gate;
   ga.gate_want = gate_want;
   if (wide || s8) {
-    ensure_l2_persisting(dev, stream);
+    l2.raise(dev, stream, gemm_state_sums_bytes(dev));
     // pairs long enough for the pacing handshake to be negligible
     if (pace_slack() > 0 && k_pad >= 2048) {
       ga.pace = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(state) +

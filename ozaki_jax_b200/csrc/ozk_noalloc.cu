@@ -9,15 +9,26 @@
 // a workspace for the BF16 slices and exponents; this variant takes it from a
 // fixed device array compiled into the library instead.
 //
+// What runs: the same extraction kernels as ozk_matmul_f64 and, because the
+// array holds no GEMM state scratch, the slice GEMM's 128-wide BF16 tiles
+// that keep their running sums in TMEM (products with at most 16 columns use
+// the int8 skinny kernel).  Sums are exact fixed-point integers either way,
+// so C is bit-identical to ozk_matmul_f64 with OZK_ACC_FIXED.
+//
 // The scratch is a file-scope __device__ array of OZK_NOALLOC_SCRATCH_BYTES
 // (32 MiB).  Every GPU that loads the library holds it until the process
-// exits.  That bounds the problem size: the slice workspace of an N x K by
-// K x M product with (n_hi, n_lo) slices must fit (1024 x 1024 x 1024 at
-// precision 'high' does); larger requests are refused with OZK_ERR_WORKSPACE.
+// exits.  That bounds the problem size: the slices-only workspace of an
+// N x K by K x M product with (n_hi, n_lo) slices must fit, i.e.
+//   align256(2 nS N k_pad) + align256(2 nS M k_pad) + align256(4 nS N)
+//   + align256(4 nS M) + align256(8 K M) + 256 <= 32 MiB,
+// nS = n_hi + n_lo, k_pad = K rounded up to 64 (1024 x 1024 x 1024 at
+// precision 'high' fits); larger requests are refused with OZK_ERR_WORKSPACE.
 // Host code never hands the array's name to a kernel (on the host it is only
-// a stand-in for the symbol); its device address is looked up once per device
-// with cudaGetSymbolAddress on that device's first call, so the first call on
-// a device should come before any stream capture.  All calls on a device share
+// a stand-in for the symbol); its device address is looked up with
+// cudaGetSymbolAddress in the current context on every call (a cheap lookup),
+// so nothing goes stale when a caller switches or recreates contexts.  The
+// first call in a context also loads the library's module there, so it
+// should come before any stream capture.  All calls on a device share
 // the one array and it keeps the last call's contents: nothing in it needs to
 // start at zero (the extraction kernels write every slice element, padding
 // included, and every exponent before the GEMM reads them), but calls whose
@@ -33,20 +44,13 @@ namespace {
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[OZK_NOALLOC_SCRATCH_BYTES];
 
-void* g_scratch_addr[64] = {nullptr};  // per device, from cudaGetSymbolAddress
-
-int scratch_for_current_device(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return ozk::set_cuda_error("cudaGetDevice", e);
-  if (dev < 0 || dev >= 64) return ozk::set_error(OZK_ERR_ARG, "device index %d out of range", dev);
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p) return ozk::set_cuda_error("cudaGetSymbolAddress(scratch)", e);
-    g_scratch_addr[dev] = p;
-  }
-  *out = g_scratch_addr[dev];
+// The array's address in the current context.  A __device__ symbol's address
+// belongs to a context, not to a device index, so it is not cached.
+int scratch_for_current_context(void** out) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p) return ozk::set_cuda_error("cudaGetSymbolAddress(scratch)", e);
+  *out = p;
   return OZK_OK;
 }
 
@@ -68,7 +72,7 @@ extern "C" int ozk_matmul_f64_noalloc(const double* A, int64_t lda, const double
                           (long long)N, (long long)K, (long long)M, n_hi, n_lo, need,
                           (int)OZK_NOALLOC_SCRATCH_BYTES);
   void* scratch = nullptr;
-  int rc = scratch_for_current_device(&scratch);
+  int rc = scratch_for_current_context(&scratch);
   if (rc) return rc;
   return ozk_matmul_f64(A, lda, B, ldb, C, ldc, N, K, M, -1, n_hi, n_lo, OZK_ACC_FIXED, scratch,
                         (size_t)OZK_NOALLOC_SCRATCH_BYTES, status_dev, stream);

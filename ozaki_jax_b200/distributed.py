@@ -67,6 +67,47 @@ def _pairs(lib, n_hi, n_lo):
     return pa, pb, n
 
 
+def _meta_device(dev, group):
+    """Device for small host-logic collectives: the compute device under NCCL,
+    the CPU under gloo."""
+    return dev if dist.get_backend(group) == "nccl" else torch.device("cpu")
+
+
+def _agree(err, values, dev, group):
+    """Every rank contributes `err` (a message, or None when its arguments are
+    valid) and a list of int64 `values`; one all_gather gives every rank all of
+    them.  If any rank's arguments are invalid, every rank raises ValueError
+    before the first data collective, so no rank is left waiting in one.
+    Returns the gathered values, one list per rank."""
+    world = dist.get_world_size(group)
+    mdev = _meta_device(dev, group)
+    mine = torch.tensor([1 if err else 0] + [int(v) for v in values], dtype=torch.int64,
+                        device=mdev)
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(parts, mine, group=group)
+    rows = [p.tolist() for p in parts]
+    bad = [r for r, row in enumerate(rows) if row[0]]
+    if bad:
+        raise ValueError(err if err else f"invalid arguments on rank(s) {bad}")
+    return [row[1:] for row in rows]
+
+
+_FLAG_BITS = 8
+
+
+def _or_status(status, group):
+    """Bitwise OR of the OZK_FLAG_* words of all ranks (collectives have no OR:
+    the bits are spread into words and reduced with MAX), written back into
+    `status` in place.  Every rank then raises for a bad value in any rank's
+    operands, as the single-GPU call does."""
+    mdev = _meta_device(status.device, group)
+    bits = ((status.to(mdev).view(1) >> torch.arange(_FLAG_BITS, device=mdev)) & 1).to(torch.int32)
+    dist.all_reduce(bits, op=dist.ReduceOp.MAX, group=group)
+    word = int((bits.to(torch.int64) << torch.arange(_FLAG_BITS, device=mdev)).sum().item())
+    status.fill_(word)
+    return word
+
+
 def matmul_rowsharded(A_local, B, K=None, precision="high", b_source="replicated", group=None):
     """C_local = (A @ B)[rows of this rank] with the Ozaki 'fused' accumulation.
 
@@ -81,19 +122,25 @@ def matmul_rowsharded(A_local, B, K=None, precision="high", b_source="replicated
     nS = n_hi + n_lo
     dev = A_local.device
     rank = dist.get_rank(group)
-    Ad = A_local.to(dtype=torch.float64).contiguous()
-    nb, Kd = Ad.shape
+    # arguments are checked on every rank and agreed on before any data moves
+    err = None
     if b_source not in ("replicated", "root"):
-        raise ValueError("b_source must be 'replicated' or 'root'")
-    shape = torch.tensor(list(B.shape) if (B is not None and rank == 0) else [0, 0],
-                         dtype=torch.int64, device=dev)
+        err = "b_source must be 'replicated' or 'root'"
+    elif A_local.dim() != 2:
+        err = f"A_local must be 2-D, got shape {tuple(A_local.shape)}"
+    elif (b_source == "replicated" or rank == 0) and (B is None or B.dim() != 2):
+        err = "B must be a 2-D tensor on " + ("every rank" if b_source == "replicated"
+                                              else "rank 0")
+    nb, Kd = tuple(A_local.shape) if A_local.dim() == 2 else (0, 0)
+    Kb, M = tuple(B.shape) if (err is None and B is not None and B.dim() == 2) else (-1, -1)
+    meta = _agree(err, [nb, Kd, Kb, M], dev, group)
     if b_source == "root":
-        dist.broadcast(shape, src=0, group=group)
-        Kb, M = int(shape[0]), int(shape[1])
-    else:
-        Kb, M = B.shape
-    if Kb != Kd:
-        raise ValueError(f"Incompatible shapes for matmul: {tuple(Ad.shape)} and {(Kb, M)}.")
+        Kb, M = meta[0][2], meta[0][3]
+    bad = [r for r, (_, kd, _, _) in enumerate(meta) if kd != Kb]
+    if bad:
+        raise ValueError(f"Incompatible shapes for matmul: A_local has {meta[bad[0]][1]} columns "
+                         f"on rank {bad[0]}, B is {(Kb, M)}.")
+    Ad = A_local.to(dtype=torch.float64).contiguous()
     rho = compute_rho_f32(Kd)
     sh = D.stream_handle(dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -106,11 +153,7 @@ def matmul_rowsharded(A_local, B, K=None, precision="high", b_source="replicated
 
     # int8 slice codes (exact for rho >= 19) when every rank's GEMM can take them;
     # the ranks agree on the format of B's slices before any is broadcast.
-    use_s8 = rho >= 19 and M >= 256
-    if use_s8:
-        nbmin = torch.tensor([nb], dtype=torch.int64, device=dev)
-        dist.all_reduce(nbmin, op=dist.ReduceOp.MIN, group=group)
-        use_s8 = int(nbmin.item()) >= 256
+    use_s8 = rho >= 19 and M >= 256 and min(row[0] for row in meta) >= 256
     if use_s8:
         k8 = (Kd + 127) // 128 * 128
         fail = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -162,11 +205,13 @@ def matmul_rowsharded(A_local, B, K=None, precision="high", b_source="replicated
                                        eB.data_ptr(), nS, nb, M, k_pad, pa, pb, npairs,
                                        L.OZK_ACC_FIXED, 0, 1.0, 0.0, None, 0, C.data_ptr(), M,
                                        None, GW.data_ptr(), GW.numel(), rho, status.data_ptr(), sh))
-    flags = int(status.item())
+    # B's flags live on the ranks that extracted it: every rank raises together
+    flags = _or_status(status, group)
+    if flags & L.OZK_FLAG_TIMEOUT:
+        raise L.OzakiError(L.OZK_ERR_TIMEOUT, "a device-side wait exceeded its time budget")
     if flags:
-        raise ValueError("Ozaki preflight marked this input as unsafe: inputs contain NaN or Inf"
-                         if flags & (L.OZK_FLAG_NONFINITE | L.OZK_FLAG_RANGE)
-                         else f"device status {flags}")
+        from .matmul import _flags_reasons, _PREFIX
+        raise ValueError(_PREFIX + "; ".join(_flags_reasons(flags)))
     return C
 
 
@@ -187,12 +232,17 @@ def matmul_rowsharded_host(A_local, B, precision="high", group=None):
     n_hi, n_lo = _resolve_precision(precision)
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    dev = torch.device("cuda", torch.cuda.current_device())
+    dev = (torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available()
+           else torch.device("cpu"))
     A = np.ascontiguousarray(A_local, dtype=np.float64)
     Bh = np.asarray(B, dtype=np.float64)
+    err = None
     if A.ndim != 2 or Bh.ndim != 2 or A.shape[1] != Bh.shape[0]:
-        raise ValueError(f"Incompatible shapes for matmul: {A.shape} and {Bh.shape}.")
-    K, M = Bh.shape
+        err = f"Incompatible shapes for matmul: {A.shape} and {Bh.shape}."
+    K, M = Bh.shape if Bh.ndim == 2 else (-1, -1)
+    meta = _agree(err, [K, M], dev, group)
+    if any(row != [K, M] for row in meta):
+        raise ValueError(f"B must have the same shape on every rank; got {[tuple(r) for r in meta]}")
     kc = (K + world - 1) // world
     k0, k1 = min(K, rank * kc), min(K, (rank + 1) * kc)
     share = torch.zeros((kc, M), dtype=torch.float64, device=dev)
@@ -203,6 +253,7 @@ def matmul_rowsharded_host(A_local, B, precision="high", group=None):
     Bd = gathered[:K]
     nb = A.shape[0]
     if nb == 0 or M == 0:
+        _or_status(torch.zeros(1, dtype=torch.int32, device=dev), group)  # same steps as the others
         return np.zeros((nb, M))
     # A and C stay on the host: the host-buffer pipeline streams them in row
     # blocks over PCIe while the blocks before are computed; B is read from
@@ -216,10 +267,12 @@ def matmul_rowsharded_host(A_local, B, precision="high", group=None):
         A.ctypes.data, K, Bd.data_ptr(), M, Ch.ctypes.data, M, nb, K, M, compute_rho_f32(K),
         n_hi, n_lo, L.OZK_ACC_FIXED, 0, ws.data_ptr(), ws_bytes, ctypes.byref(flags),
         D.stream_handle(dev)))
-    if flags.value & L.OZK_FLAG_TIMEOUT:
+    # a bad value in any rank's rows makes every rank raise, as one GPU would
+    word = _or_status(torch.tensor([flags.value], dtype=torch.int32, device=dev), group)
+    if word & L.OZK_FLAG_TIMEOUT:
         raise L.OzakiError(L.OZK_ERR_TIMEOUT, "a device-side wait exceeded its time budget")
-    if flags.value:
-        raise ValueError(_PREFIX + "; ".join(_flags_reasons(flags.value)))
+    if word:
+        raise ValueError(_PREFIX + "; ".join(_flags_reasons(word)))
     return Ch
 
 
@@ -254,13 +307,18 @@ def gram_rowsharded(A_local, precision="high", group=None):
     nS = n_hi + n_lo
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
+    dev = A_local.device
+    err = None if A_local.dim() == 2 else f"A_local must be 2-D, got shape {tuple(A_local.shape)}"
+    n_loc, K = tuple(A_local.shape) if err is None else (0, -1)
+    meta = _agree(err, [n_loc, K], dev, group)
+    if any(row[1] != K for row in meta):
+        raise ValueError(f"A_local must have the same column count on every rank; got "
+                         f"{[row[1] for row in meta]}")
     Ad = A_local.to(dtype=torch.float64).contiguous()
-    dev = Ad.device
-    n_loc, K = Ad.shape
-    counts = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(world)]
-    dist.all_gather(counts, torch.tensor([n_loc], dtype=torch.int64, device=dev), group=group)
-    counts = [int(c.item()) for c in counts]
+    counts = [row[0] for row in meta]
     N = sum(counts)
+    if N < 1:
+        raise ValueError("gram needs at least one row")
     cols = [row_range(K, r, world) for r in range(world)]
     c0, c1 = cols[rank]
     kr = c1 - c0
@@ -335,7 +393,9 @@ def gram_rowsharded(A_local, precision="high", group=None):
 
     if not (use_s8 and slices_and_gemm(True)):
         slices_and_gemm(False)
-    flags = int(status.item())
+    flags = _or_status(status, group)
+    if flags & L.OZK_FLAG_TIMEOUT:
+        raise L.OzakiError(L.OZK_ERR_TIMEOUT, "a device-side wait exceeded its time budget")
     if flags:
         raise ValueError(_PREFIX + "; ".join(_flags_reasons(flags)))
     return G

@@ -30,7 +30,9 @@ def gram(A, precision="high", accumulation="bf16_interleaved", mode="f64"):
     mode='f64': native FP64 product on the device, (G + G^T) / 2.
     mode='ozaki': Ozaki product from the B200 kernels (rho from the row count,
     ozaki_jax/gram.py:92-95); accumulation 'bf16_interleaved' and 'fused'
-    both run the FP64-epilogue kernel.
+    both run the exact int64 fixed-point epilogue (each element's pair
+    products summed exactly, rounded to FP64 once) on the tiles on or above
+    the diagonal, each written mirrored, so G is exactly symmetric.
     """
     allowed_modes = {"f64", "ozaki"}
     if mode not in allowed_modes:

@@ -39,3 +39,43 @@ def test_reference_arm_other_ranks_are_silent():
                    "--warmup", "1"], {"RANK": "1", "WORLD_SIZE": "2"})
     assert r.returncode == 0, r.stderr
     assert r.stdout.strip() == ""
+
+
+def test_parity_blocks_are_blocks_of_the_full_reference_result():
+    """bench.py's parity report runs the oracle on blocks of the full-size
+    input.  That is only valid because rows of A and columns of B (lines of A
+    for gram) are extracted independently: a block of the oracle's output on
+    the block's rows and columns must equal that block of the full result,
+    bit for bit.  Checked here on small cases of each kind."""
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    import bench
+    import ozaki_oracle as O
+    rng = np.random.RandomState(5)
+    A, B = rng.randn(300, 1000), rng.randn(1000, 520)
+    blocks = bench.sample_blocks(300, 520, rows=64, cols=256)
+    assert blocks == [(0, 64, 0, 256), (236, 300, 264, 520)]
+    fused, numpy_, exact = bench.reference_blocks("matmul", {"A": A, "B": B}, blocks, 4, 1)
+    full_f = O.fused_ondevice(A, B, 4, 1)[2]
+    full_n = O.ondevice_numpy(A, B, 4, 1)
+    for (r0, r1, c0, c1), f, nn in zip(blocks, fused, numpy_):
+        assert np.array_equal(f, full_f[r0:r1, c0:c1])
+        assert np.array_equal(nn, full_n[r0:r1, c0:c1])
+    # gram: G = (P + P^T) / 2, P = ozaki(A^T, A)
+    G = rng.randn(1500, 300) * np.exp(rng.randn(1, 300))
+    gb = bench.sample_blocks(300, 300, rows=40, cols=100)
+    fused, _, exact = bench.reference_blocks("gram", {"A": G}, gb, 4, 1)
+    full = O.gram_ozaki(G, 4, 1)
+    for (r0, r1, c0, c1), f in zip(gb, fused):
+        assert np.array_equal(f, full[r0:r1, c0:c1])
+    # residual: b - ozaki(A, x)
+    X, Bv = rng.randn(1000, 16), rng.randn(300, 16)
+    rb = bench.sample_blocks(300, 16, rows=64, cols=256)
+    fused, _, _ = bench.reference_blocks("residual", {"A": A, "x": X, "b": Bv}, rb, 4, 1)
+    full = O.residual_ozaki(A, X, Bv, 4, 1)
+    for (r0, r1, c0, c1), f in zip(rb, fused):
+        assert np.array_equal(f, full[r0:r1, c0:c1])
+    # the report on the reference's own blocks: ratio 1
+    rep = bench.parity_report("matmul", {"A": A, "B": B},
+                              [full_f[r0:r1, c0:c1] for r0, r1, c0, c1 in blocks], blocks, 4, 1)
+    assert rep["within_1p5x_ref"] and rep["rel_err_ours"] == rep["rel_err_ref_fused"]

@@ -71,3 +71,57 @@ def test_row_range_partition():
             assert all(b[1] == c[0] for b, c in zip(blocks, blocks[1:]))
             sizes = [b[1] - b[0] for b in blocks]
             assert max(sizes) - min(sizes) <= 1
+
+
+def _bad_args_worker(rank, world, port, q):
+    """Rank 1 passes operands whose K does not match; every rank must raise
+    ValueError before any data collective (none may hang in one)."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    out = {}
+    try:
+        from ozaki_jax_b200.distributed import (_or_status, gram_rowsharded, matmul_rowsharded,
+                                                matmul_rowsharded_host)
+        k_a = 8 if rank == 0 else 9
+        A = torch.zeros((4, k_a), dtype=torch.float64)
+        B = torch.zeros((8, 5), dtype=torch.float64)
+        for name, call in (
+                ("replicated", lambda: matmul_rowsharded(A, B, b_source="replicated")),
+                ("root", lambda: matmul_rowsharded(A, B if rank == 0 else None, b_source="root")),
+                ("root_missing_B", lambda: matmul_rowsharded(torch.zeros((4, 8), dtype=torch.float64),
+                                                             None if rank == 0 else B,
+                                                             b_source="root")),
+                ("host", lambda: matmul_rowsharded_host(A.numpy(), B.numpy())),
+                ("gram", lambda: gram_rowsharded(torch.zeros((4, 3 + rank), dtype=torch.float64)))):
+            try:
+                call()
+                out[name] = "returned"
+            except ValueError as e:
+                out[name] = "ValueError: " + str(e)
+        # status words are OR-ed over the ranks
+        st = torch.tensor([1 if rank == 0 else 4], dtype=torch.int32)
+        out["or"] = _or_status(st, None)
+        out["or_inplace"] = int(st.item())
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bad_arguments_on_one_rank_raise_on_every_rank_gloo_world2():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bad_args_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank in (0, 1):
+        out = res[rank]
+        for name in ("replicated", "root", "root_missing_B", "host", "gram"):
+            assert out[name].startswith("ValueError"), (rank, name, out[name])
+        assert out["or"] == 5 and out["or_inplace"] == 5

@@ -219,7 +219,8 @@ int ozk_matmul_f64(const double* A, int64_t lda, const double* B, int64_t ldb, d
  * the result comes back to the host): A, B, C are host pointers (pinned memory
  * copies at full DMA speed; pageable memory works through the driver's
  * staging); any of them may also be device memory of this GPU (unified
- * addressing picks the copy direction).  The copies overlap the compute: B is copied and column-extracted
+ * addressing picks the copy direction; pageable host arrays go through the
+ * page-locked staging of ozk_memcpy_staged).  The copies overlap the compute: B is copied and column-extracted
  * first, then A and C move in row blocks of block_rows rows (0 = automatic) on
  * two internal copy streams while the previous block's slice GEMM runs on
  * `stream`.  Blocking: returns after C is written; *status_host receives the
@@ -232,6 +233,16 @@ int ozk_matmul_f64_hostbuf(const double* A, int64_t lda, const double* B, int64_
                            int64_t ldc, int64_t N, int64_t K, int64_t M, int rho, int n_hi,
                            int n_lo, int acc_mode, int64_t block_rows, void* workspace,
                            size_t ws_bytes, int32_t* status_host, void* stream);
+
+/* Host <-> device copy of `bytes` (no counterpart in the reference: the
+ * reference's jnp.asarray / np.asarray transfers, ozaki_jax/matmul.py:803-821).
+ * One of dst, src is device memory of the current GPU, the other host memory.
+ * Pageable host memory goes through the library's page-locked staging ring
+ * with host memcpy threads (the driver's own staging of pageable memory is
+ * several times slower than PCIe); page-locked host memory is copied
+ * directly.  Blocking: returns when the copy is complete (after the work
+ * already on `stream`). */
+int ozk_memcpy_staged(void* dst, const void* src, size_t bytes, void* stream);
 
 /* Allocation-free variant of ozk_matmul_f64 (acc_mode OZK_ACC_FIXED, rho from K).
  * It has no counterpart in the reference.  For callers that must not allocate
@@ -311,18 +322,17 @@ int ozk_selftest_timeout(int budget_ms, int32_t* status_dev, int32_t* ok_dev, vo
 /* L2 residency of the slice GEMM's running sums (no counterpart in the
  * reference).  The 256-wide GEMM tiles keep per-CTA running sums in a global
  * scratch (ozk_slice_gemm_workspace_bytes, about 38 MB) that it re-reads every
- * pair, and it marks those accesses evict_last.  That priority takes effect
- * only inside the context's persisting-L2 set-aside, so around each 256-wide
- * launch the library raises the set-aside to hold the sums and puts the
- * previous limit back as soon as the kernel is enqueued: the caller's other
- * kernels keep their own setting.  (OZK_L2_PERSIST=0 in the environment
- * leaves the limit alone, OZK_L2_PERSIST=<MB> asks for that size, and
- * OZK_L2_PERSIST=sticky raises it once per device and keeps it.)  This call
- * sets the limit explicitly: `bytes` (clamped to the device maximum; 0 turns
- * it off; (size_t)-1 only queries), the value in force before goes to
- * *previous (may be NULL).  The limit belongs to this process's CUDA context
- * and ends with it; lines not marked persisting may use the set-aside while no
- * persisting data holds it. */
+ * pair, and it marks those accesses evict_last, a priority that takes effect
+ * inside the context's persisting-L2 set-aside.  The library does not change
+ * that limit by default (the context's own set-aside, 23.7 MB on B200, keeps
+ * the GEMM within 2.5% of one that holds all the sums).  Opt-ins:
+ * OZK_L2_PERSIST=sticky in the environment raises it once per device to hold
+ * the sums, OZK_L2_PERSIST=<MB> to that size; or this call sets it
+ * explicitly: `bytes` (clamped to the device maximum; 0 turns it off;
+ * (size_t)-1 only queries), the value in force before goes to *previous (may
+ * be NULL).  The limit belongs to this process's CUDA context and ends with
+ * it; lines not marked persisting may use the set-aside while no persisting
+ * data holds it. */
 int ozk_set_l2_persisting(size_t bytes, size_t* previous);
 /* Library version string. */
 const char* ozk_version(void);

@@ -44,9 +44,13 @@ def to_device_f64(x, device):
     a = np.ascontiguousarray(x, dtype=np.float64)
     host = torch.from_numpy(a)
     if a.nbytes >= (1 << 20) and not host.is_pinned():
-        pinned = torch.empty(host.shape, dtype=torch.float64, pin_memory=True)
-        pinned.copy_(host)
-        host = pinned
+        # pageable: the library's page-locked staging with host memcpy threads
+        from . import _lib as L
+        out = torch.empty(a.shape, dtype=torch.float64, device=device)
+        with torch.cuda.device(device):
+            L.check(L.load().ozk_memcpy_staged(out.data_ptr(), a.ctypes.data, a.nbytes,
+                                               stream_handle(device)))
+        return out
     return host.to(device, non_blocking=True)
 
 

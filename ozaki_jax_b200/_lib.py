@@ -71,6 +71,7 @@ SIGNATURES = {
     "ozk_matmul_f64_hostbuf": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64, c_int,
                                        c_int, c_int, c_int, c_i64, vp, c_size, vp, vp]),
     "ozk_set_l2_persisting": (c_int, [c_size, vp]),
+    "ozk_memcpy_staged": (c_int, [vp, vp, c_size, vp]),
     "ozk_matmul_f64_noalloc": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64,
                                        c_int, c_int, vp, vp]),
     "ozk_matmul_host_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_int]),

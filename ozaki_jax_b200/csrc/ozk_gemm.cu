@@ -949,46 +949,37 @@ static int pace_slack() {
 }
 
 // The running sums are marked evict_last; that priority applies inside the
-// context's persisting-L2 set-aside.  Measured on B200 at 8192^3 with int8
-// slices: with a set-aside that holds them, DRAM writes of the GEMM drop from
-// 11.7 GB to 0.5 GB.  The set-aside is a limit of the whole CUDA context, so
-// by default it is raised only around the library's own launch: the limit in
-// force before is put back as soon as the kernel is enqueued, and the caller's
-// other kernels see their own setting.  OZK_L2_PERSIST=0 leaves the limit
-// alone, OZK_L2_PERSIST=<MB> asks for that size (still restored), and
-// OZK_L2_PERSIST=sticky raises it once per device and keeps it (the behaviour
-// of earlier versions, kept for comparisons).
+// context's persisting-L2 set-aside.  The set-aside is a limit of the whole
+// CUDA context, so the library leaves it as the caller has it: with the
+// context's own limit (23.7 MB on this pool's B200s) the 8192^3 slice GEMM
+// measured within 2.5% of a set-aside that holds all the sums, while changing
+// the limit around each launch (and putting it back) stalled the overlapped
+// copy pipelines (cudaDeviceSetLimit waits for the device).  Opt-ins:
+// OZK_L2_PERSIST=sticky raises it once per device to hold the sums (about
+// 46 MB) and keeps it, OZK_L2_PERSIST=<MB> raises it once to that size;
+// ozk_set_l2_persisting sets it explicitly.
 struct L2Scope {
-  bool restore = false;
-  size_t prev = 0;
   void raise(int dev, cudaStream_t stream, size_t sums_bytes) {
-    static int sticky_done[64] = {0};
+    static int done[64] = {0};
     const char* env = getenv("OZK_L2_PERSIST");
-    const bool sticky = env && strcmp(env, "sticky") == 0;
+    if (!env || dev < 0 || dev >= 64 || done[dev]) return;
     size_t want = sums_bytes + (8u << 20);
-    if (env && !sticky) {
+    if (strcmp(env, "sticky") != 0) {
       const long mb = atol(env);
       if (mb <= 0) return;
       want = (size_t)mb << 20;
     }
-    if (sticky && (dev < 0 || dev >= 64 || sticky_done[dev])) return;
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
-      return;  // a limit change is not a capturable operation
+      return;  // a limit change is not a capturable operation; try a later launch
+    done[dev] = 1;
     size_t cur = 0;
     int mx = 0;
     if (cudaDeviceGetLimit(&cur, cudaLimitPersistingL2CacheSize) != cudaSuccess ||
         cudaDeviceGetAttribute(&mx, cudaDevAttrMaxPersistingL2CacheSize, dev) != cudaSuccess)
       return;
     if (want > (size_t)mx) want = (size_t)mx;
-    if (sticky) sticky_done[dev] = 1;
-    if (cur >= want) return;
-    if (cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, want) != cudaSuccess) return;
-    restore = !sticky;
-    prev = cur;
-  }
-  ~L2Scope() {
-    if (restore) cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, prev);
+    if (cur < want) cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, want);
   }
 };
 
@@ -1020,7 +1011,7 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
                          size_t state_bytes, int rho, int32_t* status, bool s8,
                          const int32_t* gate, int gate_want, cudaStream_t stream) {
   if (N == 0 || M == 0) return OZK_OK;
-  L2Scope l2;  // a raised persisting-L2 limit is put back when this returns
+  L2Scope l2;  // the persisting-L2 opt-ins (OZK_L2_PERSIST)
   if (n_pairs < 1 || n_pairs > OZK_MAX_PAIRS) return set_error(OZK_ERR_ARG, "n_pairs out of range");
   if (k_pad <= 0 || k_pad % OZK_KB) return set_error(OZK_ERR_ARG, "k_pad must be a positive multiple of 64");
   if (s8 && !slice_gemm_s8_eligible(N, M, k_pad, mode, rho, state_bytes))

@@ -16,10 +16,19 @@
 // host until the last copy has been issued.  The copies use unified
 // addressing, so any of A, B and C may also be device memory (a B already
 // gathered on this GPU is copied on the device, not over PCIe).
+//
+// Ordinary pageable host arrays (what a NumPy caller passes) are moved through
+// the library's page-locked staging ring with host memcpy threads
+// (ozk_staging.cu): the H2D side stages B, then each block of A, enqueueing
+// each block's compute as soon as its rows are on their way; a pageable C is
+// copied out by a helper thread block by block as each block's GEMM finishes,
+// while the calling thread is still staging later blocks of A.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <condition_variable>
 #include <mutex>
+#include <thread>
 #include <vector>
 
 #include "ozaki_b200.h"
@@ -132,6 +141,60 @@ int64_t pick_block_rows(int64_t N, int64_t block_rows) {
 
 int n_pairs_of(int n_hi, int n_lo) { return n_hi * n_hi + 2 * n_hi * n_lo; }
 
+// The helper thread that copies C's blocks out to pageable memory: block b is
+// taken once the calling thread has enqueued its compute (enqueued(b + 1)).
+// finish(abort) waits for the thread; with abort set it stops before the
+// blocks not yet enqueued.  Returns the thread's first error.
+class BlockCopyOut {
+ public:
+  template <class F>
+  void start(int dev, int nblk, F copy_block) {
+    th_ = std::thread([this, dev, nblk, copy_block] {
+      cudaSetDevice(dev);
+      for (int b = 0; b < nblk; ++b) {
+        {
+          std::unique_lock<std::mutex> lk(mu_);
+          cv_.wait(lk, [&] { return abort_ || enqueued_ > b; });
+          if (enqueued_ <= b) return;  // aborted before this block was enqueued
+        }
+        const int rc = copy_block(b);
+        if (rc) {
+          std::lock_guard<std::mutex> lk(mu_);
+          if (!rc_) rc_ = rc;
+          return;
+        }
+      }
+    });
+  }
+  void enqueued(int n) {
+    if (!th_.joinable()) return;
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      enqueued_ = n;
+    }
+    cv_.notify_all();
+  }
+  int finish(bool abort) {
+    if (!th_.joinable()) return OZK_OK;
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      if (abort) abort_ = true;
+    }
+    cv_.notify_all();
+    th_.join();
+    return rc_;
+  }
+  ~BlockCopyOut() { finish(true); }
+
+ private:
+  std::thread th_;
+  std::mutex mu_;
+  std::condition_variable cv_;
+  int enqueued_ = 0;
+  bool abort_ = false;
+  int rc_ = OZK_OK;
+};
+
 }  // namespace
 
 extern "C" size_t ozk_matmul_hostbuf_workspace_bytes(int64_t N, int64_t K, int64_t M, int n_hi,
@@ -179,6 +242,11 @@ extern "C" int ozk_matmul_f64_hostbuf(const double* A, int64_t lda, const double
   cudaStream_t s = (cudaStream_t)stream;
   CopyStreams cs;
   if ((rc = copy_streams(&cs))) return rc;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return set_error(OZK_ERR_CUDA, "cudaGetDevice failed");
+  const bool a_pageable = is_pageable(A), b_pageable = is_pageable(B);
+  const bool c_pageable = is_pageable(C);
+  BlockCopyOut d2h;
 
   // Events: entry, B ready, A block ready x nblk, C block ready x nblk, copies done x 2.
   std::vector<cudaEvent_t> ev(4 + 2 * (size_t)nblk, nullptr);
@@ -228,26 +296,32 @@ extern "C" int ozk_matmul_f64_hostbuf(const double* A, int64_t lda, const double
   } while (0)
 
   OZK_TRY_CUDA(cudaMemsetAsync(w.status, 0, 4, s), "cudaMemsetAsync(status)");
+  OZK_TRY_CUDA(cudaMemsetAsync(w.gate, 0, 4, s), "cudaMemsetAsync(gate)");
   OZK_TRY_CUDA(cudaEventRecord(ev_entry, s), "cudaEventRecord");
   OZK_TRY_CUDA(cudaStreamWaitEvent(cs.h2d, ev_entry, 0), "cudaStreamWaitEvent");
   OZK_TRY_CUDA(cudaStreamWaitEvent(cs.d2h, ev_entry, 0), "cudaStreamWaitEvent");
 
-  // Host -> device: B, then the row blocks of A.
-  OZK_TRY_CUDA(cudaMemcpy2DAsync(w.B, (size_t)M * 8, B, (size_t)ldb * 8, (size_t)M * 8, (size_t)K,
-                                 cudaMemcpyDefault, cs.h2d),
-               "cudaMemcpy2DAsync(B)");
-  OZK_TRY_CUDA(cudaEventRecord(ev_b, cs.h2d), "cudaEventRecord");
-  for (int b = 0; b < nblk; ++b) {
-    const int64_t r0 = b * br, nb = (r0 + br <= N ? br : N - r0);
-    OZK_TRY_CUDA(cudaMemcpy2DAsync(w.A + r0 * K, (size_t)K * 8, A + r0 * lda, (size_t)lda * 8,
-                                   (size_t)K * 8, (size_t)nb, cudaMemcpyDefault, cs.h2d),
-                 "cudaMemcpy2DAsync(A)");
-    OZK_TRY_CUDA(cudaEventRecord(ev_a[b], cs.h2d), "cudaEventRecord");
+  // A pageable C is copied out by a helper thread, block by block, as each
+  // block's compute is enqueued and then finished.
+  if (c_pageable) {
+    d2h.start(dev, nblk, [&, C](int b) -> int {
+      const int64_t r0 = b * br, nb = (r0 + br <= N ? br : N - r0);
+      cudaError_t e = cudaStreamWaitEvent(cs.d2h, ev_c[b], 0);
+      if (e != cudaSuccess) return set_cuda_error("cudaStreamWaitEvent", e);
+      return staged_d2h_2d(C + r0 * ldc, (size_t)ldc * 8, w.C + r0 * M, (size_t)M * 8,
+                           (size_t)M * 8, (size_t)nb, cs.d2h);
+    });
   }
-  OZK_TRY_CUDA(cudaEventRecord(ev_h2d_done, cs.h2d), "cudaEventRecord");
 
-  // Compute on the caller's stream.
-  OZK_TRY_CUDA(cudaMemsetAsync(w.gate, 0, 4, s), "cudaMemsetAsync(gate)");
+  // Host -> device: B first, then its column extraction.
+  if (b_pageable)
+    OZK_TRY(staged_h2d_2d(w.B, (size_t)M * 8, B, (size_t)ldb * 8, (size_t)M * 8, (size_t)K,
+                          cs.h2d));
+  else
+    OZK_TRY_CUDA(cudaMemcpy2DAsync(w.B, (size_t)M * 8, B, (size_t)ldb * 8, (size_t)M * 8,
+                                   (size_t)K, cudaMemcpyDefault, cs.h2d),
+                 "cudaMemcpy2DAsync(B)");
+  OZK_TRY_CUDA(cudaEventRecord(ev_b, cs.h2d), "cudaEventRecord");
   OZK_TRY_CUDA(cudaStreamWaitEvent(s, ev_b, 0), "cudaStreamWaitEvent");
   if (s8)
     OZK_TRY(launch_extract_cols_s8(w.B, M, K, M, rho, n_hi, n_lo, (int8_t*)w.SB, k8, w.eB, w.status,
@@ -255,8 +329,17 @@ extern "C" int ozk_matmul_f64_hostbuf(const double* A, int64_t lda, const double
   else
     OZK_TRY(launch_extract_cols(w.B, M, K, M, rho, n_hi, n_lo, w.SB, k_pad, w.eB, w.status, w.BT,
                                 s));
+  // Then block by block: the rows of A, and the block's compute behind them.
   for (int b = 0; b < nblk; ++b) {
     const int64_t r0 = b * br, nb = (r0 + br <= N ? br : N - r0);
+    if (a_pageable)
+      OZK_TRY(staged_h2d_2d(w.A + r0 * K, (size_t)K * 8, A + r0 * lda, (size_t)lda * 8,
+                            (size_t)K * 8, (size_t)nb, cs.h2d));
+    else
+      OZK_TRY_CUDA(cudaMemcpy2DAsync(w.A + r0 * K, (size_t)K * 8, A + r0 * lda, (size_t)lda * 8,
+                                     (size_t)K * 8, (size_t)nb, cudaMemcpyDefault, cs.h2d),
+                   "cudaMemcpy2DAsync(A)");
+    OZK_TRY_CUDA(cudaEventRecord(ev_a[b], cs.h2d), "cudaEventRecord");
     uint16_t* SA = w.SA + (size_t)nS * r0 * k_pad;
     int32_t* eA = w.eA + (size_t)nS * r0;
     double* Cb = w.C + r0 * M;
@@ -277,40 +360,45 @@ extern "C" int ozk_matmul_f64_hostbuf(const double* A, int64_t lda, const double
       OZK_TRY(launch_slice_gemm_ex(SA, eA, nS, w.SB, w.eB, nS, nb, M, k_pad, pa, pb, np,
                                    OZK_ACC_FIXED, 0, 1.0, 0.0, nullptr, 0, Cb, M, nullptr, w.state,
                                    w.state_bytes, rho, w.status, false, w.gate, 1, s));
-      OZK_TRY_CUDA(cudaEventRecord(ev_c[b], s), "cudaEventRecord");
-      continue;
-    }
-    OZK_TRY(launch_extract_rows(w.A + r0 * K, K, nb, K, rho, n_hi, n_lo, SA, k_pad, eA, w.status,
-                                s));
-    if (!prod) {
-      OZK_TRY(launch_slice_gemm(SA, eA, nS, w.SB, w.eB, nS, nb, M, k_pad, pa, pb, np, acc_mode, 0,
-                                1.0, 0.0, nullptr, 0, Cb, M, nullptr, w.state, w.state_bytes, rho,
-                                w.status, s));
     } else {
-      OZK_TRY(launch_slice_gemm(SA, eA, nS, w.SB, w.eB, nS, nb, M, k_pad, pa, pb, np,
-                                OZK_ACC_PRODUCTS, 0, 1.0, 0.0, nullptr, 0, nullptr, 0, w.products,
-                                nullptr, 0, rho, w.status, s));
-      OZK_TRY(launch_accumulate_2sum(w.products, eA, w.eB, nb, M, n_hi, n_lo, nullptr, nullptr, Cb,
-                                     M, s));
+      OZK_TRY(launch_extract_rows(w.A + r0 * K, K, nb, K, rho, n_hi, n_lo, SA, k_pad, eA,
+                                  w.status, s));
+      if (!prod) {
+        OZK_TRY(launch_slice_gemm(SA, eA, nS, w.SB, w.eB, nS, nb, M, k_pad, pa, pb, np, acc_mode,
+                                  0, 1.0, 0.0, nullptr, 0, Cb, M, nullptr, w.state, w.state_bytes,
+                                  rho, w.status, s));
+      } else {
+        OZK_TRY(launch_slice_gemm(SA, eA, nS, w.SB, w.eB, nS, nb, M, k_pad, pa, pb, np,
+                                  OZK_ACC_PRODUCTS, 0, 1.0, 0.0, nullptr, 0, nullptr, 0,
+                                  w.products, nullptr, 0, rho, w.status, s));
+        OZK_TRY(launch_accumulate_2sum(w.products, eA, w.eB, nb, M, n_hi, n_lo, nullptr, nullptr,
+                                       Cb, M, s));
+      }
     }
     OZK_TRY_CUDA(cudaEventRecord(ev_c[b], s), "cudaEventRecord");
+    d2h.enqueued(b + 1);
   }
 
-  // Device -> host, block by block as each GEMM finishes.  Issued after all
-  // compute so that a copy into pageable memory (which the driver may carry out
-  // synchronously) cannot hold back the next block's launches.
-  for (int b = 0; b < nblk; ++b) {
-    const int64_t r0 = b * br, nb = (r0 + br <= N ? br : N - r0);
-    OZK_TRY_CUDA(cudaStreamWaitEvent(cs.d2h, ev_c[b], 0), "cudaStreamWaitEvent");
-    OZK_TRY_CUDA(cudaMemcpy2DAsync(C + r0 * ldc, (size_t)ldc * 8, w.C + r0 * M, (size_t)M * 8,
-                                   (size_t)M * 8, (size_t)nb, cudaMemcpyDefault, cs.d2h),
-                 "cudaMemcpy2DAsync(C)");
+  // Device -> host into page-locked or device memory: block by block as each
+  // GEMM finishes, issued after all compute.
+  if (!c_pageable) {
+    for (int b = 0; b < nblk; ++b) {
+      const int64_t r0 = b * br, nb = (r0 + br <= N ? br : N - r0);
+      OZK_TRY_CUDA(cudaStreamWaitEvent(cs.d2h, ev_c[b], 0), "cudaStreamWaitEvent");
+      OZK_TRY_CUDA(cudaMemcpy2DAsync(C + r0 * ldc, (size_t)ldc * 8, w.C + r0 * M, (size_t)M * 8,
+                                     (size_t)M * 8, (size_t)nb, cudaMemcpyDefault, cs.d2h),
+                   "cudaMemcpy2DAsync(C)");
+    }
   }
 
 done:
 #undef OZK_TRY
 #undef OZK_TRY_CUDA
   {
+    // the copy-out thread finishes (or gives up after an error) before the
+    // workspace and the events go
+    const int rc_d2h = d2h.finish(rc != OZK_OK);
+    if (!rc) rc = rc_d2h;
     // Whatever happened, the copy streams must be finished with the workspace
     // (and with the caller's host buffers) before it is released and before we
     // return.

@@ -108,6 +108,17 @@ int launch_accumulate_2sum_scaled(const float* products, const float* col_scales
                                   const float* row_scales, const int32_t* group_sizes,
                                   int n_groups, const int32_t* block_ends, int n_blocks, int64_t N,
                                   int64_t M, float* C_hi, float* C_lo, cudaStream_t stream);
+// Pageable host memory (neither page-locked, registered, managed nor device).
+bool is_pageable(const void* p);
+// Copies between pageable host memory and the device through the library's
+// page-locked staging ring with host memcpy threads (ozk_staging.cu), rows of
+// `width` bytes with the given pitches, ordered on `s`.  staged_h2d_2d returns
+// once the source has been read (DMAs may still run on s); staged_d2h_2d
+// returns when the destination holds the data.
+int staged_h2d_2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
+                  size_t rows, cudaStream_t s);
+int staged_d2h_2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t width,
+                  size_t rows, cudaStream_t s);
 int launch_accumulate_2sum(const float* products, const int32_t* eA, const int32_t* eB, int64_t N,
                            int64_t M, int n_hi, int n_lo, float* C_hi, float* C_lo, double* C,
                            int64_t ldc, cudaStream_t stream);

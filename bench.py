@@ -12,8 +12,13 @@ slice extraction of A and B, then the persistent slice-pair GEMM with the
 exact fixed-point epilogue, and every other launch the operator makes (the
 gated BF16 recomputation, which exits at once when the int8 codes were exact).
 The operator's kernels are also launched one by one in a second timed loop,
-for the per-kernel split and the roofline of the slice GEMM.  Multi-GPU:
-rank r owns rows [r N/P, (r+1) N/P) of A and C; timing is the max over ranks.
+for the per-kernel split and the roofline of the slice GEMM.  Multi-GPU
+(torchrun, one rank per GPU): the step is the multi-GPU C-ABI operator
+ozk_matmul_f64_multi; rank r owns rows [r N/P, (r+1) N/P) of A and C and, by
+default (--b-source columns), columns [r mc, (r+1) mc) of B, mc = ceil(M/P):
+each rank extracts its columns and the int8 slice stacks are all-gathered over
+NCCL inside every step (the root broadcast and the replicated extraction are
+timed too and reported under b_source_modes); timing is the max over ranks.
 Inputs exceed L2 (126 MB), so no flush is needed between steps.
 
 Rank 0 prints one JSON line.  `value` is FP64-equivalent TFLOP/s (2NKM/t)
@@ -509,6 +514,25 @@ def ours(args):
             _lib.check(lib.ozk_matmul_f64(Ad.data_ptr(), k, Bd.data_ptr(), m, C.data_ptr(), m, nb,
                                           k, m, -1, n_hi, n_lo, _lib.OZK_ACC_FIXED, ws.data_ptr(),
                                           ws.numel(), st.data_ptr(), sh))
+        if world > 1:
+            # the multi-GPU operator: B's slices reach every rank inside the step
+            from ozaki_jax_b200 import distributed as dd
+            mctx = dd.context()
+            c0, c1 = dd.column_range(m, rank, world)
+            Bcols = Bd[:, c0:c1].contiguous()
+            Pv, I64 = ctypes.c_void_p, ctypes.c_int64
+            b_args = {"columns": (Bcols, c1 - c0), "root": (Bd if rank == 0 else None, m),
+                      "replicated": (Bd, m)}
+
+            def multi_op(mode):
+                Bm, ldb = b_args[mode]
+                args_ = (mctx.ptr, (Pv * 1)(Ad.data_ptr()), (I64 * 1)(k),
+                         (Pv * 1)(Bm.data_ptr() if Bm is not None else None), (I64 * 1)(ldb),
+                         (Pv * 1)(C.data_ptr()), (I64 * 1)(m), n, k, m, n_hi, n_lo,
+                         dd._B_MODES[mode], _lib.OZK_MULTI_NOWAIT, (Pv * 1)(sh),
+                         (Pv * 1)(st.data_ptr()))
+                return lambda: _lib.check(lib.ozk_matmul_f64_multi(*args_))
+            op = multi_op(args.b_source)
     elif kind == "gram":
         A = W["A"]
         n, k = A.shape
@@ -565,6 +589,25 @@ def ours(args):
     barrier()
     op_ms = t_start.elapsed_time(t_end) / args.steps
     assert st.item() == 0, f"device status {st.item()}"
+    b_modes = None
+    if world > 1 and kind == "matmul":
+        # the other ways of bringing B to every rank, each in its own timed loop
+        b_modes = {}
+        for mode in ("columns", "root", "replicated"):
+            if mode == args.b_source:
+                b_modes[mode] = op_ms
+                continue
+            f = multi_op(mode)
+            for _ in range(2):
+                f()
+            barrier()
+            b_modes[mode] = _timed(f, args.steps, stream)
+        t = torch.tensor([b_modes[x] for x in ("columns", "root", "replicated")],
+                         dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        b_modes = {x: {"ms_per_step": v, "value": flops / (v * 1e-3) / 1e12}
+                   for x, v in zip(("columns", "root", "replicated"), t.tolist())}
+        assert st.item() == 0, f"device status {st.item()}"
 
     # ---- the same kernels launched one by one, for the per-kernel split
     breakdown, gemm_ms, extract_ms, kernel_launches = None, None, None, 0
@@ -712,12 +755,17 @@ def ours(args):
 
     l2_prev = ctypes.c_size_t(0)
     _lib.check(lib.ozk_set_l2_persisting(ctypes.c_size_t(-1).value, ctypes.byref(l2_prev)))
+    if world > 1:
+        from ozaki_jax_b200.distributed import close_contexts
+        close_contexts()
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
         return
     bf16_peak, hbm_peak, src = peaks()
     op_launches = {"matmul": 7, "gram": 5, "residual": 7}[kind] if s8 else 3
+    if world > 1:
+        op_launches = 5  # extract A rows, transpose + extract B's columns, flags, GEMM
     out = {
         "metric": METRIC if name == "c2" else (
             "FP64-equiv TFLOP/s (2NK^2/t)" if kind == "gram" else "FP64-equiv TFLOP/s (2MNK/t)"),
@@ -730,11 +778,19 @@ def ours(args):
                    "N": n, "K": k, "M": m, "precision": precision, "rho": rho,
                    "slices": "int8 codes" if s8 else "bf16",
                    "parallelism": f"row-blocks x{world}" if kind == "matmul" else "1 GPU",
-                   "timed": "ozk_matmul_f64 (the C-ABI operator, all its launches)"
+                   "timed": (f"ozk_matmul_f64_multi (the C-ABI multi-GPU operator), "
+                             f"b_source={args.b_source}: B's int8 slices "
+                             + {"columns": "all-gathered from per-rank column blocks",
+                                "root": "broadcast from rank 0",
+                                "replicated": "extracted on every rank (no exchange)"}[
+                                 args.b_source] + " over NCCL inside every step"
+                             if world > 1 else
+                             "ozk_matmul_f64 (the C-ABI operator, all its launches)")
                             if kind == "matmul" else f"ozk_{kind}_f64 (the C-ABI operator)",
                    "l2": "inputs larger than L2 (126 MB), no flush",
                    "l2_persisting_mb_after": round(l2_prev.value / 2**20, 1)},
         "parity": parity,
+        "b_source_modes": b_modes,
         "rel_err_vs_cublas_dgemm": rel_err_dgemm,
         "dgemm_fp64_tflops": dgemm_tflops,
         "breakdown_ms": {"operator": op_ms, "extract": extract_ms, "slice_gemm": gemm_ms,
@@ -877,6 +933,9 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2",
                     help="c2 (default): the headline 8192^3 line; others: the remaining "
                          "benchmark configurations on one GPU")
+    ap.add_argument("--b-source", choices=["columns", "root", "replicated"], default="columns",
+                    help="--gpus > 1: how B's slices reach every rank in the timed operator "
+                         "(all three are timed and reported)")
     ap.add_argument("--cpu-baseline", action="store_true",
                     help="also time the CPU oracle for a workload other than c2")
     ap.add_argument("--case", default=None,

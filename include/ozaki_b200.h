@@ -269,6 +269,62 @@ int ozk_matmul_f64_noalloc(const double* A, int64_t lda, const double* B, int64_
                            int64_t ldc, int64_t N, int64_t K, int64_t M, int n_hi, int n_lo,
                            int32_t* status_dev, void* stream);
 
+/* ---------------------------------------------------------------- multi-GPU */
+
+/* A set of GPUs that compute one product together (no counterpart in the
+ * reference, which has no multi-device code; this partitions the on-device
+ * operators _fully_fused_f64_jit / _bf16_interleaved_f64_jit,
+ * ozaki_jax/matmul.py:514-540, across the GPUs of one node).  It holds one
+ * NCCL communicator per local GPU and per-GPU workspaces grown on demand;
+ * NCCL (libnccl.so.2) is loaded at run time.  Two ways to make one:
+ *   - one process per GPU: every rank calls ozk_context_create_rank with the
+ *     same OZK_NCCL_ID_BYTES id, made by ozk_nccl_unique_id on one rank and
+ *     passed to the others by the caller (an MPI broadcast, a torch.distributed
+ *     store, a file, ...);
+ *   - one process driving several GPUs (the JAX model): ozk_context_create_local
+ *     with the device list; global rank i is devices[i]. */
+#define OZK_NCCL_ID_BYTES 128
+typedef struct ozk_context ozk_context;
+int ozk_nccl_unique_id(void* id_out, size_t len);
+int ozk_context_create_rank(ozk_context** ctx, int nranks, int rank, const void* nccl_id,
+                            size_t id_len, int device);
+int ozk_context_create_local(ozk_context** ctx, int ndev, const int* devices);
+int ozk_context_destroy(ozk_context* ctx);
+/* Global rank count, the global rank of the first local GPU, local GPU count. */
+int ozk_context_info(const ozk_context* ctx, int* nranks, int* first_rank, int* nlocal);
+
+/* How B reaches every rank in ozk_matmul_f64_multi. */
+#define OZK_B_REPLICATED 0 /* every rank holds all of B (K x M) and extracts it */
+#define OZK_B_ROOT 1       /* rank 0 holds B; its slices are broadcast over NCCL */
+#define OZK_B_COLUMNS 2    /* rank r holds columns [r mc, min(M, (r+1) mc)) of B,
+                              mc = ceil(M / P), as a K x m_r matrix; slices all-gathered */
+/* Flags of ozk_matmul_f64_multi. */
+#define OZK_MULTI_NOWAIT 0x1 /* do not wait for the result (see below) */
+#define OZK_MULTI_BF16 0x2   /* BF16 slices even where int8 codes are exact */
+/* Status bit: the int8 pass of a NOWAIT call found a slice without an exact
+ * int8 code on some rank, so C was not written; repeat the call with
+ * OZK_MULTI_BF16 (every rank sees this bit, so all repeat together). */
+#define OZK_FLAG_REDO 0x8
+
+/* C = A @ B row-sharded over the context's P global ranks (matmul(...,
+ * pipeline='ondevice', accumulation='fused') on the whole A): global rank r
+ * holds rows [r N / P, (r+1) N / P) of A (lda) and of C (ldc).  Arrays are
+ * indexed by local GPU (ozk_context_info's nlocal entries): A[i], B[i], C[i]
+ * are device pointers on that GPU, streams[i] its stream (NULL array: the
+ * legacy default streams), status_dev[i] a device word receiving the OZK_FLAG_*
+ * bits of ALL ranks (NULL array or entry: not reported).  Each rank's rows of
+ * C are bit-identical to the same rows of ozk_matmul_f64 with OZK_ACC_FIXED.
+ * All ranks must make the same calls in the same order, on the same streams
+ * from one call to the next (the workspace is reused).  Without
+ * OZK_MULTI_NOWAIT the call waits for the result (watching NCCL; after
+ * OZK_NCCL_TIMEOUT_MS, default 300 s, or an NCCL failure the communicators are
+ * aborted and the context is unusable) and runs a BF16 pass itself if an
+ * int8 code failed; with it, the call returns once everything is enqueued. */
+int ozk_matmul_f64_multi(ozk_context* ctx, const double* const* A, const int64_t* lda,
+                         const double* const* B, const int64_t* ldb, double* const* C,
+                         const int64_t* ldc, int64_t N, int64_t K, int64_t M, int n_hi, int n_lo,
+                         int b_mode, int flags, void* const* streams, int32_t* const* status_dev);
+
 /* The FP64 host pipeline (matmul(pipeline='host'), ozaki_jax/matmul.py:823-851):
  * FP64 extraction into n_slices slices, triangular pairs, FP64 accumulation,
  * all on the device.  rho < 0 selects _compute_rho(K). */

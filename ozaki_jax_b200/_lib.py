@@ -22,6 +22,14 @@ OZK_ERR_UNSUPPORTED = -8
 OZK_FLAG_NONFINITE = 0x1
 OZK_FLAG_TIMEOUT = 0x2
 OZK_FLAG_RANGE = 0x4
+OZK_FLAG_REDO = 0x8
+
+OZK_B_REPLICATED = 0
+OZK_B_ROOT = 1
+OZK_B_COLUMNS = 2
+OZK_MULTI_NOWAIT = 0x1
+OZK_MULTI_BF16 = 0x2
+OZK_NCCL_ID_BYTES = 128
 
 OZK_ACC_F64 = 0
 OZK_ACC_PRODUCTS = 1
@@ -72,6 +80,13 @@ SIGNATURES = {
                                        c_int, c_int, c_int, c_i64, vp, c_size, vp, vp]),
     "ozk_set_l2_persisting": (c_int, [c_size, vp]),
     "ozk_memcpy_staged": (c_int, [vp, vp, c_size, vp]),
+    "ozk_nccl_unique_id": (c_int, [vp, c_size]),
+    "ozk_context_create_rank": (c_int, [vp, c_int, c_int, vp, c_size, c_int]),
+    "ozk_context_create_local": (c_int, [vp, c_int, vp]),
+    "ozk_context_destroy": (c_int, [vp]),
+    "ozk_context_info": (c_int, [vp, vp, vp, vp]),
+    "ozk_matmul_f64_multi": (c_int, [vp, vp, vp, vp, vp, vp, vp, c_i64, c_i64, c_i64, c_int,
+                                     c_int, c_int, c_int, vp, vp]),
     "ozk_matmul_f64_noalloc": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64,
                                        c_int, c_int, vp, vp]),
     "ozk_matmul_host_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_int]),

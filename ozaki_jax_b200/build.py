@@ -60,7 +60,7 @@ def build(verbose=False, force=False):
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = LIB + ".tmp"
-    cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs]
+    cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-ldl", "-lpthread"]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

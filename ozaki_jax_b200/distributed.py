@@ -4,16 +4,19 @@ The reference has no multi-device code; this is the build's partitioning of
 the on-device path.  Rank r owns rows [r*N/P, (r+1)*N/P) of A and of C.  Row
 extraction is row-local, so each rank's slices of A are bit-identical to the
 single-GPU ones and each rank's block of C equals the corresponding rows of
-the single-GPU result.  B reaches every rank in one of two ways:
+the single-GPU result.  B reaches every rank in one of three ways:
 
   b_source='replicated'  every rank was given B and extracts its column slices
-                         locally (no collective in the data path);
+                         locally (no exchange of B);
   b_source='root'        rank 0 extracts B's slices once and broadcasts the slice
                          stack (int8 codes where exact, else BF16) and exponents
-                         over NCCL (NVLink).
+                         over NCCL (NVLink);
+  b_source='columns'     rank r holds columns column_range(M, r, P) of B, extracts
+                         them, and the slice stacks are all-gathered over NCCL.
 
-The collectives go through torch.distributed (NCCL for CUDA tensors, gloo on
-CPU); the compute is libozaki_b200.
+matmul_rowsharded runs the library's multi-GPU operator (ozk_matmul_f64_multi
+on an ozk_context with its own NCCL communicator); argument agreement and the
+other helpers use torch.distributed (NCCL for CUDA tensors, gloo on CPU).
 """
 
 import ctypes
@@ -60,13 +63,6 @@ def gather_rows(C_local, n_total, dst=None, group=None):
     return torch.cat([p[: r1 - r0] for p, (r0, r1) in zip(parts, sizes)], dim=0)
 
 
-def _pairs(lib, n_hi, n_lo):
-    pa = (ctypes.c_uint8 * 256)()
-    pb = (ctypes.c_uint8 * 256)()
-    n = L.check(lib.ozk_pair_schedule_snake(n_hi, n_lo, pa, pb, 256))
-    return pa, pb, n
-
-
 def _meta_device(dev, group):
     """Device for small host-logic collectives: the compute device under NCCL,
     the CPU under gloo."""
@@ -108,105 +104,148 @@ def _or_status(status, group):
     return word
 
 
-def matmul_rowsharded(A_local, B, K=None, precision="high", b_source="replicated", group=None):
-    """C_local = (A @ B)[rows of this rank] with the Ozaki 'fused' accumulation.
+class MultiContext:
+    """The library's multi-GPU context (ozk_context) for this process's GPU in a
+    torch.distributed job: one NCCL communicator over the ranks of `group`,
+    made from an id that rank 0 creates and the process group broadcasts."""
 
-    A_local: this rank's row block of A (CUDA float64, rows x K).
-    B: the full K x M matrix on every rank ('replicated'), or a K x M tensor
-       whose contents matter only on rank 0 ('root'; other ranks may pass a
-       tensor of the right shape or None with K given through A_local).
-    Returns this rank's rows of C (CUDA float64).  All ranks must call it.
+    def __init__(self, group=None):
+        lib = L.load()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.cuda.current_device()
+        idbuf = ctypes.create_string_buffer(L.OZK_NCCL_ID_BYTES)
+        err = None
+        if self.rank == 0:
+            rc = lib.ozk_nccl_unique_id(idbuf, L.OZK_NCCL_ID_BYTES)
+            err = None if rc == 0 else L.detail()
+        box = [bytes(idbuf.raw) if err is None else None, err]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group else 0,
+                                   group=group)
+        if box[1] is not None:
+            raise L.OzakiError(L.OZK_ERR_NCCL, box[1])
+        idbuf = ctypes.create_string_buffer(box[0], L.OZK_NCCL_ID_BYTES)
+        self.ptr = ctypes.c_void_p()
+        L.check(lib.ozk_context_create_rank(ctypes.byref(self.ptr), self.world, self.rank, idbuf,
+                                            L.OZK_NCCL_ID_BYTES, self.device))
+
+    def close(self):
+        if self.ptr:
+            L.check(L.load().ozk_context_destroy(self.ptr))
+            self.ptr = ctypes.c_void_p()
+
+
+_CONTEXTS = {}
+
+
+def context(group=None):
+    """The cached MultiContext of `group` on the current GPU (created by a
+    collective call on first use: every rank must ask for it together)."""
+    key = (id(group), torch.cuda.current_device())
+    if key not in _CONTEXTS:
+        _CONTEXTS[key] = MultiContext(group)
+    return _CONTEXTS[key]
+
+
+def close_contexts():
+    """Destroys the cached contexts (call on every rank before
+    destroy_process_group)."""
+    for c in _CONTEXTS.values():
+        c.close()
+    _CONTEXTS.clear()
+
+
+_B_MODES = {"replicated": L.OZK_B_REPLICATED, "root": L.OZK_B_ROOT, "columns": L.OZK_B_COLUMNS}
+
+
+def column_range(m, rank, world):
+    """Columns [c0, c1) of an m-column B held by `rank` with b_source='columns':
+    blocks of ceil(m / world) columns, the last one shorter."""
+    mc = (m + world - 1) // world
+    return min(m, rank * mc), min(m, (rank + 1) * mc)
+
+
+def matmul_rowsharded(A_local, B, precision="high", b_source="replicated", group=None):
+    """C_local = (A @ B)[rows of this rank] with the Ozaki 'fused' accumulation,
+    through the library's multi-GPU operator (ozk_matmul_f64_multi, NCCL).
+
+    A_local: this rank's row block of A (CUDA float64), rows row_range(N, r, P).
+    B: 'replicated': the full K x M matrix on every rank;
+       'root': the full matrix on rank 0 (other ranks may pass None); its slice
+               stack and exponents are broadcast;
+       'columns': this rank's columns column_range(M, r, P) of B (K x m_r); the
+               slice stacks are all-gathered.
+    Returns this rank's rows of C (CUDA float64), bit-identical to the same rows
+    of the single-GPU result.  All ranks must call it.
     """
     lib = L.load()
     n_hi, n_lo = _resolve_precision(precision)
-    nS = n_hi + n_lo
     dev = A_local.device
     rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
     # arguments are checked on every rank and agreed on before any data moves
     err = None
-    if b_source not in ("replicated", "root"):
-        err = "b_source must be 'replicated' or 'root'"
+    if b_source not in _B_MODES:
+        err = f"b_source must be one of {sorted(_B_MODES)}"
     elif A_local.dim() != 2:
         err = f"A_local must be 2-D, got shape {tuple(A_local.shape)}"
-    elif (b_source == "replicated" or rank == 0) and (B is None or B.dim() != 2):
-        err = "B must be a 2-D tensor on " + ("every rank" if b_source == "replicated"
-                                              else "rank 0")
+    elif (b_source != "root" or rank == 0) and (B is None or B.dim() != 2):
+        err = "B must be a 2-D tensor on " + ("rank 0" if b_source == "root" else "every rank")
     nb, Kd = tuple(A_local.shape) if A_local.dim() == 2 else (0, 0)
-    Kb, M = tuple(B.shape) if (err is None and B is not None and B.dim() == 2) else (-1, -1)
-    meta = _agree(err, [nb, Kd, Kb, M], dev, group)
-    if b_source == "root":
-        Kb, M = meta[0][2], meta[0][3]
-    bad = [r for r, (_, kd, _, _) in enumerate(meta) if kd != Kb]
+    Kb, Mb = tuple(B.shape) if (err is None and B is not None and B.dim() == 2) else (-1, -1)
+    meta = _agree(err, [nb, Kd, Kb, Mb], dev, group)
+    N = sum(row[0] for row in meta)
+    if any(row[0] != row_range(N, r, world)[1] - row_range(N, r, world)[0]
+           for r, row in enumerate(meta)):
+        raise ValueError(f"A's row blocks must follow row_range({N}, rank, {world}); got "
+                         f"{[row[0] for row in meta]}")
+    if b_source == "columns":
+        M = sum(row[3] for row in meta)
+        want = [column_range(M, r, world)[1] - column_range(M, r, world)[0] for r in range(world)]
+        if [row[3] for row in meta] != want:
+            raise ValueError(f"B's column blocks must follow column_range({M}, rank, {world}): "
+                             f"{want}; got {[row[3] for row in meta]}")
+        holders = range(world)
+    elif b_source == "root":
+        M = meta[0][3]
+        holders = [0]
+    else:
+        M = meta[0][3]
+        if any(row[3] != M for row in meta):
+            raise ValueError("B must have the same shape on every rank")
+        holders = range(world)
+    K = meta[0][1]
+    bad = [r for r, row in enumerate(meta) if row[1] != K or (r in holders and row[2] != K)]
     if bad:
         raise ValueError(f"Incompatible shapes for matmul: A_local has {meta[bad[0]][1]} columns "
-                         f"on rank {bad[0]}, B is {(Kb, M)}.")
+                         f"and B {meta[bad[0]][2]} rows on rank {bad[0]}.")
+    if K < 1 or M < 1:
+        raise ValueError(f"K and M must be >= 1 (got K={K}, M={M})")
+    ctx = context(group)
     Ad = A_local.to(dtype=torch.float64).contiguous()
-    rho = compute_rho_f32(Kd)
-    sh = D.stream_handle(dev)
-    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    Bd = (B.to(device=dev, dtype=torch.float64).contiguous()
+          if (B is not None and rank in holders) else None)
     C = torch.empty((nb, M), dtype=torch.float64, device=dev)
-    pa, pb, npairs = _pairs(lib, n_hi, n_lo)
-    GW = torch.empty(lib.ozk_slice_gemm_workspace_bytes(), dtype=torch.uint8, device=dev)
-    have_b = b_source == "replicated" or rank == 0
-    Bd = B.to(device=dev, dtype=torch.float64).contiguous() if have_b else None
-    BT = torch.empty((M, Kd), dtype=torch.float64, device=dev) if have_b else None
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    P = ctypes.c_void_p
+    I64 = ctypes.c_int64
 
-    # int8 slice codes (exact for rho >= 19) when every rank's GEMM can take them;
-    # the ranks agree on the format of B's slices before any is broadcast.
-    use_s8 = rho >= 19 and M >= 256 and min(row[0] for row in meta) >= 256
-    if use_s8:
-        k8 = (Kd + 127) // 128 * 128
-        fail = torch.zeros(1, dtype=torch.int32, device=dev)
-        SB = torch.empty((nS, M, k8), dtype=torch.int8, device=dev)
-        eB = torch.empty((nS, M), dtype=torch.int32, device=dev)
-        if have_b:
-            L.check(lib.ozk_extract_cols_s8_f64(Bd.data_ptr(), Bd.stride(0), Kd, M, rho, n_hi,
-                                                n_lo, SB.data_ptr(), k8, eB.data_ptr(),
-                                                BT.data_ptr(), BT.numel() * 8, fail.data_ptr(),
-                                                status.data_ptr(), sh))
-        if b_source == "root":
-            dist.broadcast(SB, src=0, group=group)
-            dist.broadcast(eB, src=0, group=group)
-            dist.broadcast(fail, src=0, group=group)
-        SA = torch.empty((nS, nb, k8), dtype=torch.int8, device=dev)
-        eA = torch.empty((nS, nb), dtype=torch.int32, device=dev)
-        L.check(lib.ozk_extract_rows_s8_f64(Ad.data_ptr(), Ad.stride(0), nb, Kd, rho, n_hi, n_lo,
-                                            SA.data_ptr(), k8, eA.data_ptr(), fail.data_ptr(),
-                                            status.data_ptr(), sh))
-        # a code without an exact int8 value anywhere sends every rank to BF16
-        dist.all_reduce(fail, op=dist.ReduceOp.MAX, group=group)
-        if int(fail.item()) == 0:
-            L.check(lib.ozk_slice_gemm_s8(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(),
-                                          eB.data_ptr(), nS, nb, M, k8, pa, pb, npairs, 0, 1.0,
-                                          0.0, None, 0, C.data_ptr(), M, GW.data_ptr(), GW.numel(),
-                                          rho, None, status.data_ptr(), sh))
-        else:
-            use_s8 = False
-        del SA, SB
-    if not use_s8:
-        k_pad = (max(Kd, 1) + 63) // 64 * 64
-        SB = torch.empty((nS, M, k_pad), dtype=torch.int16, device=dev)
-        eB = torch.empty((nS, M), dtype=torch.int32, device=dev)
-        if have_b:
-            L.check(lib.ozk_extract_cols_f64(Bd.data_ptr(), Bd.stride(0), Kd, M, rho, n_hi, n_lo,
-                                             SB.data_ptr(), k_pad, eB.data_ptr(), BT.data_ptr(),
-                                             BT.numel() * 8, status.data_ptr(), sh))
-        if b_source == "root":
-            # NCCL has no 16-bit integer type: move the BF16 bit patterns as bytes
-            dist.broadcast(SB.view(torch.uint8), src=0, group=group)
-            dist.broadcast(eB, src=0, group=group)
-        SA = torch.empty((nS, nb, k_pad), dtype=torch.int16, device=dev)
-        eA = torch.empty((nS, nb), dtype=torch.int32, device=dev)
-        if nb > 0:
-            L.check(lib.ozk_extract_rows_f64(Ad.data_ptr(), Ad.stride(0), nb, Kd, rho, n_hi, n_lo,
-                                             SA.data_ptr(), k_pad, eA.data_ptr(), status.data_ptr(),
-                                             sh))
-            L.check(lib.ozk_slice_gemm(SA.data_ptr(), eA.data_ptr(), nS, SB.data_ptr(),
-                                       eB.data_ptr(), nS, nb, M, k_pad, pa, pb, npairs,
-                                       L.OZK_ACC_FIXED, 0, 1.0, 0.0, None, 0, C.data_ptr(), M,
-                                       None, GW.data_ptr(), GW.numel(), rho, status.data_ptr(), sh))
-    # B's flags live on the ranks that extracted it: every rank raises together
-    flags = _or_status(status, group)
+    def call(flags):
+        L.check(lib.ozk_matmul_f64_multi(
+            ctx.ptr, (P * 1)(Ad.data_ptr()), (I64 * 1)(K),
+            (P * 1)(Bd.data_ptr() if Bd is not None else None),
+            (I64 * 1)(Bd.shape[1] if Bd is not None else 0), (P * 1)(C.data_ptr()), (I64 * 1)(M),
+            N, K, M, n_hi, n_lo, _B_MODES[b_source], flags, (P * 1)(D.stream_handle(dev)),
+            (P * 1)(status.data_ptr())))
+
+    call(L.OZK_MULTI_NOWAIT)
+    flags = int(status.item())  # the OZK_FLAG_* bits of every rank
+    if flags & L.OZK_FLAG_REDO:
+        # a slice had no exact int8 code on some rank: every rank sees it and
+        # repeats with BF16 slices
+        status.zero_()
+        call(L.OZK_MULTI_NOWAIT | L.OZK_MULTI_BF16)
+        flags = int(status.item())
     if flags & L.OZK_FLAG_TIMEOUT:
         raise L.OzakiError(L.OZK_ERR_TIMEOUT, "a device-side wait exceeded its time budget")
     if flags:

@@ -1,6 +1,8 @@
 """Row-sharded matmul on two GPUs over NCCL (skipped with fewer GPUs): each
-rank's rows of C equal the single-GPU result bit for bit, for B replicated
-and for B's slices broadcast from the root."""
+rank's rows of C equal the single-GPU result bit for bit, for B replicated,
+B's slices broadcast from the root and B's column blocks all-gathered (also
+with a ragged column split); a NaN in B on the root makes every rank raise;
+and one process can drive both GPUs through one context."""
 
 import os
 import queue
@@ -35,22 +37,37 @@ def _worker(rank, world, port, q):
                             timeout=timedelta(seconds=120))
     try:
         import ozaki_jax_b200 as oz
-        from ozaki_jax_b200.distributed import (gather_rows, gram_rowsharded, matmul_rowsharded,
+        from ozaki_jax_b200.distributed import (close_contexts, column_range, gather_rows,
+                                                gram_rowsharded, matmul_rowsharded,
                                                 matmul_rowsharded_host, residual_rowsharded,
                                                 row_range)
         rng = np.random.RandomState(0)
         out = {}
         # K = 700: BF16 slices; K = 5000 (rho 19, 600 rows per rank): int8 codes
-        for n, k, m in ((600, 700, 500), (1200, 5000, 600)):
+        for n, k, m in ((600, 700, 500), (1200, 5000, 601)):
             A, B = rng.randn(n, k), rng.randn(k, m)
             ref = oz.matmul(A, B, pipeline="ondevice")  # single-GPU result on this device
             r0, r1 = row_range(n, rank, world)
             Ad = torch.as_tensor(A[r0:r1]).to(dev)
-            for src in ("replicated", "root"):
-                Bd = torch.as_tensor(B).to(dev) if (src == "replicated" or rank == 0) else None
+            for src in ("replicated", "root", "columns"):
+                if src == "columns":
+                    c0, c1 = column_range(m, rank, world)  # 601 columns: 301 + 300
+                    Bd = torch.as_tensor(np.ascontiguousarray(B[:, c0:c1])).to(dev)
+                else:
+                    Bd = torch.as_tensor(B).to(dev) if (src == "replicated" or rank == 0) else None
                 C = matmul_rowsharded(Ad, Bd, b_source=src)
                 full = gather_rows(C, n)
                 out[(k, src)] = bool(np.array_equal(full.cpu().numpy(), ref))
+        # a NaN in B, held by the root only: every rank raises, as one GPU would
+        A, B = rng.randn(600, 5000), rng.randn(5000, 300)
+        B[17, 5] = np.nan
+        r0, r1 = row_range(600, rank, world)
+        try:
+            matmul_rowsharded(torch.as_tensor(A[r0:r1]).to(dev),
+                              torch.as_tensor(B).to(dev) if rank == 0 else None, b_source="root")
+            out["nan_root_raises"] = False
+        except ValueError as e:
+            out["nan_root_raises"] = "NaN" in str(e)
             # host arrays, B uploaded in shares and all-gathered over NCCL
             Ch = matmul_rowsharded_host(A[r0:r1], B)
             out[(k, "host")] = bool(np.array_equal(Ch, ref[r0:r1]))
@@ -72,6 +89,7 @@ def _worker(rank, world, port, q):
             out[("gram", n)] = bool(np.array_equal(Gr.cpu().numpy(), ref[c0:c1]))
         q.put((rank, out))
     finally:
+        close_contexts()
         dist.destroy_process_group()
 
 
@@ -96,4 +114,55 @@ def test_rowsharded_matmul_two_gpus():
         p.join(timeout=120)
         assert p.exitcode == 0
     for _, out in res:
-        assert len(out) == 9 and all(out.values()), out
+        assert len(out) == 13 and all(out.values()), out
+
+
+def _local_worker(q):
+    """One process, two GPUs, one context (ozk_context_create_local): the
+    column-block mode through the C ABI, each GPU's rows against the
+    single-GPU result."""
+    import ctypes
+    import ozaki_jax_b200 as oz
+    from ozaki_jax_b200 import _lib as L
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    lib = L.load()
+    rng = np.random.RandomState(3)
+    n, k, m = 1024, 5000, 700
+    A, B = rng.randn(n, k), rng.randn(k, m)
+    ref = oz.matmul(A, B, pipeline="ondevice")
+    ctx = ctypes.c_void_p()
+    L.check(lib.ozk_context_create_local(ctypes.byref(ctx), 2, (ctypes.c_int * 2)(0, 1)))
+    try:
+        P = ctypes.c_void_p
+        I64 = ctypes.c_int64
+        mc = (m + 1) // 2
+        As, Bs, Cs, sts = [], [], [], []
+        for g in range(2):
+            dev = torch.device("cuda", g)
+            As.append(torch.as_tensor(A[g * n // 2:(g + 1) * n // 2]).to(dev))
+            Bs.append(torch.as_tensor(np.ascontiguousarray(B[:, g * mc:min(m, (g + 1) * mc)]))
+                      .to(dev))
+            Cs.append(torch.empty((n // 2, m), dtype=torch.float64, device=dev))
+            sts.append(torch.zeros(1, dtype=torch.int32, device=dev))
+        streams = [torch.cuda.current_stream(torch.device("cuda", g)).cuda_stream
+                   for g in range(2)]
+        L.check(lib.ozk_matmul_f64_multi(
+            ctx, (P * 2)(*[a.data_ptr() for a in As]), (I64 * 2)(k, k),
+            (P * 2)(*[b.data_ptr() for b in Bs]), (I64 * 2)(*[b.shape[1] for b in Bs]),
+            (P * 2)(*[c.data_ptr() for c in Cs]), (I64 * 2)(m, m), n, k, m, 4, 1,
+            L.OZK_B_COLUMNS, 0, (P * 2)(*streams), (P * 2)(*[t.data_ptr() for t in sts])))
+        full = np.concatenate([c.cpu().numpy() for c in Cs])
+        q.put(bool(np.array_equal(full, ref)) and all(int(t.item()) == 0 for t in sts))
+    finally:
+        lib.ozk_context_destroy(ctx)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_one_process_two_gpus_local_context():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_local_worker, args=(q,))
+    p.start()
+    ok = q.get(timeout=300)
+    p.join(timeout=120)
+    assert p.exitcode == 0 and ok

@@ -839,7 +839,9 @@ def ours(args):
                   "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                   "host_memory": "pageable NumPy arrays (what a drop-in caller passes)",
                   "pinned_value": flops / (e2e_pinned_ms * 1e-3) / 1e12}
-    if name == "c2" or args.cpu_baseline:
+    # the CPU baseline runs on rank 0 at N = 1 only (torchrun limits a rank's
+    # OpenBLAS threads, and the figure does not depend on N)
+    if (name == "c2" or args.cpu_baseline) and world == 1:
         if kind == "matmul":
             cpu_v, side, cpu_dt = cpu_oracle_sample(W["A"], W["B"], n_hi, n_lo)
             out["cpu_baseline"] = {

@@ -324,15 +324,16 @@ __global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
 // refilled with the CTA's next row at once, so its DRAM transfer overlaps the
 // slice passes of this one; several CTAs per SM keep several rows in flight.
 //
-// A slice pass is one barrier: each warp posts its partial line maxima, and
-// after the barrier every warp reduces all partials of the line and derives
-// the slice parameters itself, then sweeps its registers, taking the next
-// pass's maxima on the way.  In a cluster the barrier is the cluster's, with
-// relaxed arrival (a release would wait for this thread's code stores still
-// in flight), and each partial is one 64-bit word (pass << 32) | FP32 bits:
-// a reader in any CTA of the cluster takes it once the tag matches.  Two
-// parity slots suffice, as a slot is rewritten only after the next barrier,
-// which no thread passes before its reads of the slot are done.  Slices are
+// A slice pass is one CTA barrier: each warp posts its partial line maxima,
+// and after the barrier every warp reduces all partials of the line and
+// derives the slice parameters itself, then sweeps its registers, taking the
+// next pass's maxima on the way.  In a cluster each partial is one 64-bit word
+// (pass << 32) | FP32 bits, and a reader in any CTA of the cluster takes it
+// once the tag matches (a bounded spin), so the CTAs need no cluster barrier
+// per pass.  Two parity slots suffice: a warp posts its pass-g+1 partial only
+// after reading every pass-g partial, so no CTA can reach pass g+2, and
+// rewrite a slot, before every warp of every peer has read that slot's pass-g
+// value.  Slices are
 // written as 8-byte (BF16) or 4-byte (int8) words, all columns up to k_pad
 // included; int8 codes are staged in shared memory (two buffers per side), and
 // one thread bulk-stores a pass's codes after the next barrier, which takes
@@ -552,8 +553,11 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         fence_proxy_async_smem();            // this thread's staged codes, for the bulk store
         if (tid == 0) bulk_wait_read_all();  // the buffer this pass writes is no longer read
       }
-      if constexpr (CL == 1) __syncthreads();
-      else cluster_sync_relaxed();
+      // A CTA barrier, not a cluster one: the tags carry the exchange between
+      // CTAs.  A warp posts its pass-g+1 partial only after it has read every
+      // pass-g partial, so when any CTA posts pass g+2 into a parity slot, all
+      // warps of all peers have read that slot's pass-g value.
+      __syncthreads();
       if constexpr (STAGE) {
         if (tid == 0 && pend) flush();
         pend = false;

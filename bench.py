@@ -255,15 +255,30 @@ def make_inputs(n, k, m):
     return A, B
 
 
-def make_workload(name, size=8192):
+def make_workload(name, size=8192, rank=0, world=1):
     """Host arrays of a configuration, drawn from RandomState(0):
     c2  A then B, N(0,1)                                   (size^3)
     c3  A's U(0,1), A's N(0,1), B's U(0,1), B's N(0,1); entry (U-0.5)*exp(10 N)
     c4  A N(0,1) (65536 x 4096), then column j scaled by 10^(-6j/4095)
     c5a A then B, N(0,1) (32768^2)
     c5b A N(0,1) (32768^2) + 32768 I, then x, then b (32768 x 16 each)
+    With world > 1, c5a and c5b give each rank only its rows of A (and of b):
+    a full-size draw on every rank would hold 8 x 17 GB of host memory.  Rank
+    r's rows then come from RandomState(1 + r) (N(0,1), plus the diagonal for
+    c5b); B (c5a) and x (c5b) still come from RandomState(0).  Such a dict
+    carries the global row count "n_total" and the rank's first row "row0".
     Returns a dict with the operands and the shapes."""
     rng = np.random.RandomState(0)
+    if world > 1 and name in ("c5a", "c5b"):
+        n = 32768
+        r0, r1 = rank * n // world, (rank + 1) * n // world
+        rr = np.random.RandomState(1 + rank)
+        A = rr.randn(r1 - r0, n)
+        if name == "c5a":
+            return {"A": A, "B": rng.randn(n, n), "n_total": n, "row0": r0}
+        A[np.arange(r1 - r0), r0 + np.arange(r1 - r0)] += n
+        return {"A": A, "x": rng.randn(n, 16), "b": rr.randn(r1 - r0, 16), "n_total": n,
+                "row0": r0}
     if name == "c2":
         A, B = make_inputs(size, size, size)
         return {"A": A, "B": B}
@@ -479,8 +494,6 @@ def ours(args):
     if name == "c2":
         precision = args.precision
         desc = f"matmul {args.size}^3 precision={precision}, N(0,1)"
-    if world > 1 and name != "c2":
-        raise SystemExit("--gpus > 1 runs the headline configuration (c2) only")
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
@@ -491,16 +504,17 @@ def ours(args):
     nS = n_hi + n_lo
     n_pairs = n_hi * n_hi + 2 * n_hi * n_lo
 
-    W = make_workload(name, args.size)
+    W = make_workload(name, args.size, rank, world)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
     st = torch.zeros(1, dtype=torch.int32, device=dev)
+    res = {}  # results of the multi-GPU Python operators
     if kind == "matmul":
         A, B = W["A"], W["B"]
-        n, k = A.shape
+        n, k = W.get("n_total", A.shape[0]), A.shape[1]
         m = B.shape[1]
         r0, r1 = rank * n // world, (rank + 1) * n // world
-        A_blk = np.ascontiguousarray(A[r0:r1])
+        A_blk = np.ascontiguousarray(A if "n_total" in W else A[r0:r1])
         nb = r1 - r0
         Ad = torch.as_tensor(A_blk).to(dev)
         Bd = torch.as_tensor(B).to(dev)
@@ -548,22 +562,38 @@ def ours(args):
         def op():
             _lib.check(lib.ozk_gram_f64(Ad.data_ptr(), k, C.data_ptr(), k, n, k, -1, n_hi, n_lo,
                                         ws.data_ptr(), ws.numel(), st.data_ptr(), sh))
+        if world > 1:
+            # rows of A split over the ranks; this rank's rows of G (gram_rowsharded)
+            from ozaki_jax_b200.distributed import gram_rowsharded, row_range
+            g0, g1 = row_range(n, rank, world)
+            Ad_rows = Ad[g0:g1].contiguous()
+            del Ad, C, ws
+            Ad = Ad_rows
+            c0g, c1g = row_range(k, rank, world)
+            nb = c1g - c0g
+
+            def op():
+                res["C"] = gram_rowsharded(Ad_rows, precision=precision)
     else:
         A, x, b = W["A"], W["x"], W["b"]
-        n, k = A.shape
+        n, k = W.get("n_total", A.shape[0]), A.shape[1]
         m = x.shape[1]
-        nb = n
+        nb = A.shape[0]
         Ad, Xd, bd = (torch.as_tensor(v).to(dev) for v in (A, x, b))
-        C = torch.empty((n, m), dtype=torch.float64, device=dev)
-        ws = torch.empty(lib.ozk_residual_workspace_bytes(n, k, m, n_hi, n_lo), dtype=torch.uint8,
+        # at N > 1 every rank holds its rows of A and b and all of x, and runs the
+        # operator on its rows (residual_rowsharded: rows are independent, no
+        # collective in the data path)
+        C = torch.empty((nb, m), dtype=torch.float64, device=dev)
+        ws = torch.empty(lib.ozk_residual_workspace_bytes(nb, k, m, n_hi, n_lo), dtype=torch.uint8,
                          device=dev)
         contraction = k
         flops = 2.0 * n * k * m
 
         def op():
             _lib.check(lib.ozk_residual_f64(Ad.data_ptr(), k, Xd.data_ptr(), m, bd.data_ptr(), m,
-                                            C.data_ptr(), m, n, k, m, -1, n_hi, n_lo,
+                                            C.data_ptr(), m, nb, k, m, -1, n_hi, n_lo,
                                             ws.data_ptr(), ws.numel(), st.data_ptr(), sh))
+
     rho = lib.ozk_compute_rho_f32(contraction)
     s8 = rho >= 19 and os.environ.get("OZK_S8", "1") != "0"
 
@@ -611,7 +641,8 @@ def ours(args):
 
     # ---- the same kernels launched one by one, for the per-kernel split
     breakdown, gemm_ms, extract_ms, kernel_launches = None, None, None, 0
-    if kind in ("matmul", "gram") and s8 and nb >= 256 and m >= 256:
+    if kind in ("matmul", "gram") and s8 and nb >= 256 and m >= 256 and (
+            world == 1 or kind == "matmul"):
         k8 = (contraction + 127) // 128 * 128
         fail = torch.zeros(1, dtype=torch.int32, device=dev)
         pa = (ctypes.c_uint8 * 256)()
@@ -678,6 +709,8 @@ def ours(args):
         kernel_launches = per_step * args.steps
         del SA, eA, BT
     clk = clocks.stop()
+    if "C" in res:
+        C = res["C"]
     if world > 1:
         t = torch.tensor([op_ms, gemm_ms or 0.0, extract_ms or 0.0], dtype=torch.float64,
                          device=dev)
@@ -690,23 +723,25 @@ def ours(args):
     blocks = sample_blocks(nb, m)
     Ch = [C[r0_:r1_, c0_:c1_].cpu().numpy() for r0_, r1_, c0_, c1_ in blocks]
     if kind == "matmul":
-        Wr = {"A": W["A"][r0:r1], "B": W["B"]}
+        Wr = {"A": A_blk, "B": W["B"]}
     else:
         Wr = W
     parity = parity_report(kind, Wr, Ch, blocks, n_hi, n_lo) if rank == 0 else None
 
     # ---- native FP64 (cuBLAS DGEMM) on the same operands, for comparison
+    rel_err_dgemm = dgemm_tflops = None
     if kind == "matmul":
         ref = lambda: torch.matmul(Ad, Bd)
     elif kind == "gram":
-        ref = lambda: torch.matmul(Ad.T, Ad)
+        ref = (lambda: torch.matmul(Ad.T, Ad)) if world == 1 else None
     else:
         ref = lambda: bd - torch.matmul(Ad, Xd)
-    R = ref()
-    rel_err_dgemm = float(torch.linalg.norm(C - R) / torch.linalg.norm(R))
-    del R
-    dgemm_ms = _timed(lambda: ref(), 3, stream)
-    dgemm_tflops = flops / (dgemm_ms * 1e-3) / 1e12  # every rank runs its share at once
+    if ref is not None:
+        R = ref()
+        rel_err_dgemm = float(torch.linalg.norm(C - R) / torch.linalg.norm(R))
+        del R
+        dgemm_ms = _timed(lambda: ref(), 3, stream)
+        dgemm_tflops = flops / (dgemm_ms * 1e-3) / 1e12  # every rank runs its share at once
 
     # ---- end to end through the public API, host arrays in and out
     def e2e_case(pinned):
@@ -750,8 +785,11 @@ def ours(args):
             ms = t.item()
         assert out.shape == (nb, m)
         return ms
-    e2e_ms = e2e_time(e2e_case(pinned=False))
-    e2e_pinned_ms = e2e_time(e2e_case(pinned=True))
+    # (at N > 1 the gram's and c5a's host copies would not fit eight ranks' host memory)
+    e2e_ms = e2e_pinned_ms = None
+    if world == 1 or name in ("c2", "c5b"):
+        e2e_ms = e2e_time(e2e_case(pinned=False))
+        e2e_pinned_ms = e2e_time(e2e_case(pinned=True))
 
     l2_prev = ctypes.c_size_t(0)
     _lib.check(lib.ozk_set_l2_persisting(ctypes.c_size_t(-1).value, ctypes.byref(l2_prev)))
@@ -764,7 +802,7 @@ def ours(args):
         return
     bf16_peak, hbm_peak, src = peaks()
     op_launches = {"matmul": 7, "gram": 5, "residual": 7}[kind] if s8 else 3
-    if world > 1:
+    if world > 1 and kind == "matmul":
         op_launches = 5  # extract A rows, transpose + extract B's columns, flags, GEMM
     out = {
         "metric": METRIC if name == "c2" else (
@@ -777,7 +815,7 @@ def ours(args):
                                f"accumulation={'bf16_interleaved' if kind != 'matmul' else 'fused'}",
                    "N": n, "K": k, "M": m, "precision": precision, "rho": rho,
                    "slices": "int8 codes" if s8 else "bf16",
-                   "parallelism": f"row-blocks x{world}" if kind == "matmul" else "1 GPU",
+                   "parallelism": f"row-blocks x{world}" if world > 1 else "1 GPU",
                    "timed": (f"ozk_matmul_f64_multi (the C-ABI multi-GPU operator), "
                              f"b_source={args.b_source}: B's int8 slices "
                              + {"columns": "all-gathered from per-rank column blocks",
@@ -786,7 +824,15 @@ def ours(args):
                                  args.b_source] + " over NCCL inside every step"
                              if world > 1 else
                              "ozk_matmul_f64 (the C-ABI operator, all its launches)")
-                            if kind == "matmul" else f"ozk_{kind}_f64 (the C-ABI operator)",
+                            if kind == "matmul" else (
+                                "gram_rowsharded: all-to-all of A's columns, local line "
+                                "extraction, all-gather of the slice stacks (NCCL), this rank's "
+                                "rows of G" if (kind == "gram" and world > 1) else
+                                f"ozk_{kind}_f64 (the C-ABI operator)"
+                                + (" on each rank's rows (no collective)" if world > 1 else "")),
+                   "inputs": ("each rank's rows of A (and b) from RandomState(1 + rank); "
+                              "B / x from RandomState(0)") if "n_total" in W else
+                             "RandomState(0), BASELINE's recipe",
                    "l2": "inputs larger than L2 (126 MB), no flush",
                    "l2_persisting_mb_after": round(l2_prev.value / 2**20, 1)},
         "parity": parity,
@@ -835,10 +881,13 @@ def ours(args):
         h2d, d2h = 8 * n * k, 8 * k * k
     else:
         h2d, d2h = 8 * (n * k + 2 * n * m), 8 * n * m
-    out["e2e"] = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                  "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                  "host_memory": "pageable NumPy arrays (what a drop-in caller passes)",
-                  "pinned_value": flops / (e2e_pinned_ms * 1e-3) / 1e12}
+    if e2e_ms is not None:
+        out["e2e"] = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                      "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                      "host_memory": "pageable NumPy arrays (what a drop-in caller passes)",
+                      "pinned_value": flops / (e2e_pinned_ms * 1e-3) / 1e12}
+    else:
+        out["e2e"] = None
     # the CPU baseline runs on rank 0 at N = 1 only (torchrun limits a rank's
     # OpenBLAS threads, and the figure does not depend on N)
     if (name == "c2" or args.cpu_baseline) and world == 1:

@@ -671,7 +671,7 @@ def ours(args):
                                                  1.0, 0.0, None, 0, C.data_ptr(), m, GW.data_ptr(),
                                                  GW.numel(), rho, fail.data_ptr(), st.data_ptr(),
                                                  sh))
-            per_step = 4
+            per_step = 4  # rows of A, transpose + rows of B, GEMM
         else:
             SA = torch.empty((nS, k, k8), dtype=torch.int8, device=dev)
             eA = torch.empty((nS, k), dtype=torch.int32, device=dev)
@@ -801,9 +801,12 @@ def ours(args):
             dist.destroy_process_group()
         return
     bf16_peak, hbm_peak, src = peaks()
+    # int8 path: extraction kernels (columns: transpose + rows), the slice GEMM
+    # and the gated BF16 recomputation (two extractions and a GEMM), which
+    # exits at once
     op_launches = {"matmul": 7, "gram": 5, "residual": 7}[kind] if s8 else 3
     if world > 1 and kind == "matmul":
-        op_launches = 5  # extract A rows, transpose + extract B's columns, flags, GEMM
+        op_launches = 5  # A's rows, B's transpose + rows, flags, GEMM
     out = {
         "metric": METRIC if name == "c2" else (
             "FP64-equiv TFLOP/s (2NK^2/t)" if kind == "gram" else "FP64-equiv TFLOP/s (2MNK/t)"),

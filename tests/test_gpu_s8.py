@@ -80,6 +80,40 @@ def test_codes_are_the_bf16_slices(axis, K, n_hi, n_lo):
     assert np.all(q[:, :, K:] == 0)
 
 
+@pytest.mark.parametrize("K", [700, 1024, 1025, 2048, 2049, 3000, 4096, 5000, 8192, 8193, 16384])
+@pytest.mark.parametrize("ldx", [20, 21])
+def test_column_codes_against_oracle_strided(K, ldx):
+    """int8 column codes of a strided K x 13 operand (even and odd leading
+    dimensions, a zero column) against the oracle's column extraction, from
+    short columns (rho 19 forced where the policy gives less) to 16384 rows."""
+    rng = np.random.RandomState(K + ldx)
+    cols, n_hi, n_lo = 13, 4, 1
+    Xbig = rng.randn(K, ldx) * np.exp(rng.randn(K, ldx) * 2)
+    Xbig[:, 6] = 0.0  # a zero column
+    X = Xbig[:, :cols]
+    rho = max(19, O.compute_rho_f32(K))
+    lib = L.load()
+    Xd = torch.as_tensor(Xbig).cuda()
+    k8 = (K + 127) // 128 * 128
+    codes = torch.full((5, cols, k8), 99, dtype=torch.int8, device="cuda")
+    exps = torch.empty((5, cols), dtype=torch.int32, device="cuda")
+    fail = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L.check(lib.ozk_extract_cols_s8_f64(Xd.data_ptr(), ldx, K, cols, rho, n_hi, n_lo,
+                                        codes.data_ptr(), k8, exps.data_ptr(), None, 0,
+                                        fail.data_ptr(), st.data_ptr(), stream()))
+    torch.cuda.synchronize()
+    assert fail.item() == 0 and st.item() == 0
+    hi, lo = O.double_f32_split(X)
+    sh, eh = O.extract_cols_f32(hi, rho, n_hi)
+    sl, el = O.extract_cols_f32(lo, rho, n_lo)
+    ref = np.stack([np.asarray(v, dtype=np.float64).T for v in list(sh) + list(sl)])
+    q = codes.cpu().numpy().astype(np.float64)
+    assert np.array_equal(q[:, :, :K], ref * 2.0 ** (24 - rho))
+    assert np.all(q[:, :, K:] == 0)
+    assert np.array_equal(exps.cpu().numpy(), np.stack(list(eh) + list(el)).astype(np.int32))
+
+
 @pytest.mark.parametrize("K,lines,n_hi,n_lo", [(6001, 301, 4, 1), (8192, 3, 3, 1),
                                                (4500, 1, 4, 2), (7000, 600, 4, 1)])
 def test_column_codes_odd_counts(K, lines, n_hi, n_lo):

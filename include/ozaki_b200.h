@@ -325,6 +325,26 @@ int ozk_matmul_f64_multi(ozk_context* ctx, const double* const* A, const int64_t
                          const int64_t* ldc, int64_t N, int64_t K, int64_t M, int n_hi, int n_lo,
                          int b_mode, int flags, void* const* streams, int32_t* const* status_dev);
 
+/* G = A^T A with A's rows sharded over the context's P ranks (gram(mode='ozaki')
+ * on the whole A, _gram_ozaki_jit, ozaki_jax/gram.py:19-37, with the rows
+ * split as BASELINE's multi-GPU gram asks: partial Gram blocks reduced).
+ * Global rank r holds rows [r N / P, (r+1) N / P) of A (lda); every rank
+ * receives all of G (K x K, ldg).  The lines of the gram are A's columns, split
+ * by rows over the ranks: each slice pass takes the lines' maxima over all
+ * ranks (an NCCL all-reduce of 2 K floats), so every rank's int8 codes are the
+ * single-GPU codes of its rows; each rank's symmetric int8 GEMM writes its raw
+ * int64 fixed-point sums, the sums are all-reduced exactly (NCCL int64 sum),
+ * and one kernel rounds them to FP64 and mirrors them.  Per-pair terms are
+ * rounded at 2^-36 of the top grid on each rank's partial products, so G can
+ * differ from ozk_gram_f64 in the last bit of rare elements (it is identical
+ * with one rank).  Int8 codes only (rho >= 19, N > 4096; K >= 256; at most
+ * 65536 rows per rank), else OZK_ERR_UNSUPPORTED.  If some code has no exact
+ * int8 value on any rank, G is not written and every rank's status gets
+ * OZK_FLAG_REDO.  flags: OZK_MULTI_NOWAIT as for ozk_matmul_f64_multi. */
+int ozk_gram_f64_multi(ozk_context* ctx, const double* const* A, const int64_t* lda,
+                       double* const* G, const int64_t* ldg, int64_t N, int64_t K, int n_hi,
+                       int n_lo, int flags, void* const* streams, int32_t* const* status_dev);
+
 /* The FP64 host pipeline (matmul(pipeline='host'), ozaki_jax/matmul.py:823-851):
  * FP64 extraction into n_slices slices, triangular pairs, FP64 accumulation,
  * all on the device.  rho < 0 selects _compute_rho(K). */

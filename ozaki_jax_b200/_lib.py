@@ -87,6 +87,8 @@ SIGNATURES = {
     "ozk_context_info": (c_int, [vp, vp, vp, vp]),
     "ozk_matmul_f64_multi": (c_int, [vp, vp, vp, vp, vp, vp, vp, c_i64, c_i64, c_i64, c_int,
                                      c_int, c_int, c_int, vp, vp]),
+    "ozk_gram_f64_multi": (c_int, [vp, vp, vp, vp, vp, c_i64, c_i64, c_int, c_int, c_int, vp,
+                                   vp]),
     "ozk_matmul_f64_noalloc": (c_int, [vp, c_i64, vp, c_i64, vp, c_i64, c_i64, c_i64, c_i64,
                                        c_int, c_int, vp, vp]),
     "ozk_matmul_host_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_int]),

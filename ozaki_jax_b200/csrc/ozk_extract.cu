@@ -686,6 +686,133 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
   if constexpr (CL > 1) cluster_sync();  // no peer reads this CTA's tagged slots any more
 }
 
+int upload_log2_table(int dev);  // below: the exponent rule's threshold table
+
+// ---------------------------------------------------------------- lines, one pass per launch
+
+// Line extraction split into one launch per slice pass, for lines whose
+// elements live on several GPUs (the multi-GPU gram: a column of A split by
+// rows over the ranks).  Launch t (-1 <= t < npass) re-derives every element's
+// residual from its FP64 value and the exponents of slices 0..t-1 (exps), then:
+//   t >= 0: takes the slice parameters of pass t from the line maxima gmax
+//           (the maxima over all ranks' parts of the line, [2][lines]: hi
+//           side then lo side), writes exps[t] (and exps[n_hi + t]) and the
+//           int8 codes of slice t of this rank's part (hi: slice t if t < n_hi,
+//           lo: slice n_hi + t if t < n_lo), columns n..k_pad-1 as zeros;
+//   t + 1 < npass: writes the maxima of the residual after pass t over this
+//           rank's part, pmax [2][lines], for the next launch (t = -1: of the
+//           split values themselves);
+//   t == -1: raises OZK_FLAG_NONFINITE / _RANGE for bad values (and *s8_fail).
+// The arithmetic is the row kernels' (the same split, sigma, RN sums and
+// codes), so the codes of every part are those the whole line would get from
+// one GPU once gmax is the whole line's maximum.  One CTA of kLpNT threads per
+// line (grid-stride), element e of the part at e = tid, tid + kLpNT, ...
+constexpr int kLpNT = 256;
+
+__global__ void __launch_bounds__(kLpNT) k_line_pass_s8(
+    const double* __restrict__ X, int64_t ldx, int64_t lines, int64_t n, int t, int npass,
+    int rho, int n_hi, int n_lo, const float* __restrict__ gmax, float* __restrict__ pmax,
+    int8_t* __restrict__ slices, int64_t k_pad, int32_t* __restrict__ exps, int32_t* status,
+    int32_t* s8_fail) {
+  __shared__ float s_red[2][kLpNT / 32];
+  __shared__ float s_sig[2][8];  // sigma of slices 0..t per side
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t slice_stride = lines * k_pad;
+  for (int64_t line = blockIdx.x; line < lines; line += gridDim.x) {
+    // sigma of the slices before t from their exponents, of slice t from gmax
+    if (tid < 2 * 8) {
+      const int side = tid >> 3, s = tid & 7;
+      const int ns = side == 0 ? n_hi : n_lo;
+      float sg = 0.0f;
+      if (s < t && s < ns) {
+        const int c = exps[(int64_t)(side == 0 ? s : n_hi + s) * lines + line];
+        sg = __fmul_rn(0.75f, pow2f(rho + c));
+      } else if (s == t && s < ns) {
+        float sig, inv;
+        int zero, c;
+        slice_params(gmax[side * lines + line], rho, sig, inv, zero, c);
+        sg = sig;
+        exps[(int64_t)(side == 0 ? s : n_hi + s) * lines + line] = c;
+        if (!zero && (c < -127 || rho + c > 127)) *(volatile int32_t*)s8_fail = 1;
+      }
+      s_sig[side][s] = sg;
+    }
+    __syncthreads();
+    float mh = 0.0f, ml = 0.0f;
+    int32_t flags = 0;
+    for (int64_t e = tid; e < k_pad; e += kLpNT) {
+      if (e >= n) {  // padding columns: code 0
+        if (t >= 0) {
+          if (t < n_hi) slices[(int64_t)t * slice_stride + line * k_pad + e] = 0;
+          if (t < n_lo) slices[(int64_t)(n_hi + t) * slice_stride + line * k_pad + e] = 0;
+        }
+        continue;
+      }
+      const double x = X[line * ldx + e];
+      float r[2];
+      split_f64(x, r[0], r[1]);
+      if (t < 0) {
+        if (!(fabsf(r[0]) <= 3.402823466e38f)) flags |= check_value(x, r[0]);
+      }
+#pragma unroll
+      for (int side = 0; side < 2; ++side) {
+        const int ns = side == 0 ? n_hi : n_lo;
+        for (int s = 0; s <= t && s < ns; ++s) {
+          const float sg = s_sig[side][s];
+          const float tt = __fadd_rn(r[side], sg);  // RN(r + sigma)
+          const float v = __fadd_rn(tt, -sg);       // the slice value, exact
+          r[side] = __fadd_rn(r[side], -v);         // exact
+          if (s == t)
+            slices[(int64_t)(side == 0 ? t : n_hi + t) * slice_stride + line * k_pad + e] =
+                (int8_t)(__float_as_uint(tt) - __float_as_uint(sg));
+        }
+      }
+      mh = fmaxf(mh, fabsf(r[0]));
+      ml = fmaxf(ml, fabsf(r[1]));
+    }
+    if (t < 0 && flags) {
+      raise_flag(status, flags);
+      *(volatile int32_t*)s8_fail = 1;
+    }
+    if (t + 1 < npass) {
+      // the line's maxima are >= 0 and never NaN here (fmaxf skips NaN), so
+      // their bit patterns order as unsigned integers
+      mh = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mh)));
+      ml = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ml)));
+      if (lane == 0) {
+        s_red[0][warp] = mh;
+        s_red[1][warp] = ml;
+      }
+      __syncthreads();
+      if (tid < 2) {
+        float m = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kLpNT / 32; ++w) m = fmaxf(m, s_red[tid][w]);
+        pmax[tid * lines + line] = m;
+      }
+    }
+    __syncthreads();  // s_sig and s_red are rewritten for the next line
+  }
+}
+
+int launch_line_pass_s8(const double* X, int64_t ldx, int64_t lines, int64_t n, int t, int npass,
+                        int rho, int n_hi, int n_lo, const float* gmax, float* pmax,
+                        int8_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
+                        int32_t* s8_fail, cudaStream_t stream) {
+  if (lines == 0) return OZK_OK;
+  if (n_hi > 8 || n_lo > 8) return set_error(OZK_ERR_ARG, "at most 8 slices per side");
+  int dev;
+  cudaGetDevice(&dev);
+  int rc = upload_log2_table(dev);
+  if (rc) return rc;
+  int64_t grid = lines < 65535 ? lines : 65535;
+  k_line_pass_s8<<<(unsigned)grid, kLpNT, 0, stream>>>(X, ldx, lines, n, t, npass, rho, n_hi,
+                                                      n_lo, gmax, pmax, slices, k_pad, exps,
+                                                      status, s8_fail);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? OZK_OK : set_cuda_error("k_line_pass_s8 launch", e);
+}
+
 // ---------------------------------------------------------------- transpose
 
 // XT (cols x rows, leading dimension rows) = X^T for X (rows x cols, ldx):

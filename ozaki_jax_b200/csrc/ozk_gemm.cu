@@ -90,6 +90,12 @@ struct GemmArgs {
   int dp_tiles, sk_chunks;
   long long* sk_sum;       // [tile - dp_tiles][rank][column][row in CTA]
   unsigned int* sk_count;  // [tile - dp_tiles][rank]
+  // Raw output (int8 wide tiles, fixed-point sums): with C64 set, each
+  // element's int64 sum is stored there (leading dimension ldc) as it is, in
+  // units of 2^(eA0 + eB0 + fix_scale), instead of its FP64 value in C; a
+  // symmetric launch stores only the upper triangle (column >= row).  Partial
+  // sums of a split contraction add up exactly to the whole one's.
+  long long* C64;
 };
 
 // PAIR = false: one CTA per output tile of 128 x BN.
@@ -482,6 +488,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
           // the FP64 results of a chunk's sums, alpha / beta applied, into C
           auto store_c = [&](const long long (&acc)[C2], int c0) {
             if (!rvalid) return;
+            if (g.C64) {  // the raw sums
+#pragma unroll
+              for (int j = 0; j < C2; ++j) {
+                const int64_t col = col0 + c0 + j;
+                if (col < g.M && (!g.symmetric || col >= row)) g.C64[row * g.ldc + col] = acc[j];
+              }
+              return;
+            }
             double V[C2];
 #pragma unroll
             for (int j = 0; j < C2; ++j) {
@@ -741,6 +755,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, PAIR>::THREADS, 1)
                 for (int j = 0; j < C2; ++j) {
                   const int64_t col = col0 + c0 + j;
                   if (col >= g.M) continue;
+                  if (g.C64) {  // the raw sums
+                    if (!g.symmetric || col >= row) g.C64[row * g.ldc + col] = Sa[j];
+                    continue;
+                  }
                   double v = g.alpha * fixed_value(Sa[j], eA0 + s_eB[c0 + j] + g.fix_scale);
                   if (g.beta != 0.0) v = fma(g.beta, g.Cin[row * g.ldcin + col], v);
                   if (!g.symmetric) {
@@ -1009,8 +1027,11 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
                          int symmetric, double alpha, double beta, const double* Cin,
                          int64_t ldcin, double* C, int64_t ldc, float* products, double* state,
                          size_t state_bytes, int rho, int32_t* status, bool s8,
-                         const int32_t* gate, int gate_want, cudaStream_t stream) {
+                         const int32_t* gate, int gate_want, cudaStream_t stream,
+                         long long* C64) {
   if (N == 0 || M == 0) return OZK_OK;
+  if (C64 && (!s8 || mode != OZK_ACC_FIXED))
+    return set_error(OZK_ERR_UNSUPPORTED, "raw int64 sums come from the int8 fixed-point GEMM only");
   L2Scope l2;  // the persisting-L2 opt-ins (OZK_L2_PERSIST)
   if (n_pairs < 1 || n_pairs > OZK_MAX_PAIRS) return set_error(OZK_ERR_ARG, "n_pairs out of range");
   if (k_pad <= 0 || k_pad % OZK_KB) return set_error(OZK_ERR_ARG, "k_pad must be a positive multiple of 64");
@@ -1077,6 +1098,7 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
   ga.Cin = Cin;
   ga.ldcin = ldcin;
   ga.C = C;
+  ga.C64 = C64;
   ga.ldc = ldc;
   ga.products = products;
   ga.status = status;

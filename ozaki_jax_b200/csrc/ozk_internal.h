@@ -78,7 +78,8 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
                          int symmetric, double alpha, double beta, const double* Cin,
                          int64_t ldcin, double* C, int64_t ldc, float* products, double* state,
                          size_t state_bytes, int rho, int32_t* status, bool s8,
-                         const int32_t* gate, int gate_want, cudaStream_t stream);
+                         const int32_t* gate, int gate_want, cudaStream_t stream,
+                         long long* C64 = nullptr);
 // Whether the int8 GEMM serves this request (fixed-point sums, rho >= 19,
 // 256-wide tiles with the state scratch, k_pad within the extraction limits).
 bool slice_gemm_s8_eligible(int64_t N, int64_t M, int64_t k_pad, int mode, int rho,
@@ -99,6 +100,15 @@ bool s8_enabled();
 // with s8), box of 128 bytes x box_rows, 128-byte swizzle.
 int make_slice_map(CUtensorMap* map, const void* base, int64_t k_pad, int64_t rows, int depth,
                    int box_rows, bool s8);
+// One slice pass of the int8 line extraction over this GPU's part of each
+// line (X: lines x n, ldx): t = -1 writes the part's maxima of the split
+// values to pmax [2][lines]; t >= 0 takes pass t's line maxima from gmax,
+// writes exps and the codes of slice t (and n_hi + t), and, while t + 1 <
+// npass, the part's maxima after the pass to pmax.  See k_line_pass_s8.
+int launch_line_pass_s8(const double* X, int64_t ldx, int64_t lines, int64_t n, int t, int npass,
+                        int rho, int n_hi, int n_lo, const float* gmax, float* pmax,
+                        int8_t* slices, int64_t k_pad, int32_t* exps, int32_t* status,
+                        int32_t* s8_fail, cudaStream_t stream);
 // Bytes of the per-CTA FP64 state scratch the 256-wide GEMM tiles need.
 size_t gemm_state_bytes(int dev);
 // Smallest workspace ozk_matmul_f64 (OZK_ACC_F64) accepts: without the state

@@ -41,6 +41,7 @@
 #include <vector>
 
 #include "ozaki_b200.h"
+#include "ozk_fixed.cuh"
 #include "ozk_internal.h"
 
 namespace ozk {
@@ -56,6 +57,7 @@ struct NcclApi {
   decltype(&ncclGetErrorString) GetErrorString = nullptr;
   decltype(&ncclAllGather) AllGather = nullptr;
   decltype(&ncclBroadcast) Broadcast = nullptr;
+  decltype(&ncclAllReduce) AllReduce = nullptr;
   decltype(&ncclGroupStart) GroupStart = nullptr;
   decltype(&ncclGroupEnd) GroupEnd = nullptr;
   bool ok = false;
@@ -93,6 +95,7 @@ const NcclApi& nccl() {
     OZK_SYM(GetErrorString)
     OZK_SYM(AllGather)
     OZK_SYM(Broadcast)
+    OZK_SYM(AllReduce)
     OZK_SYM(GroupStart)
     OZK_SYM(GroupEnd)
 #undef OZK_SYM
@@ -120,6 +123,40 @@ __global__ void k_reduce_flags(const int32_t* all, int nranks, int32_t* gate, in
   *gate = f;
   const int32_t add = st | (f ? redo : 0);
   if (status_out && add) atomicOr(status_out, add);
+}
+
+// G = the FP64 values of the reduced int64 sums P (upper triangle, K x K):
+// G[i][j] = G[j][i] = P[i][j] * 2^(e0[i] + e0[j] + fix_scale), 32 x 32 tiles
+// I <= J through shared memory so both writes are coalesced.  Runs only when
+// *gate == 0 (no int8 code failed on any rank).
+__global__ void __launch_bounds__(256) k_gram_finalize(const long long* __restrict__ P,
+                                                       int64_t K, const int32_t* __restrict__ e0,
+                                                       int fix_scale, const int32_t* gate,
+                                                       double* __restrict__ G, int64_t ldg) {
+  if (*(volatile const int32_t*)gate) return;
+  __shared__ double tile[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t nt = (K + 31) / 32;
+  for (int64_t b = blockIdx.x; b < nt * nt; b += gridDim.x) {
+    const int64_t ti = b / nt, tj = b % nt;
+    if (tj < ti) continue;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int64_t i = ti * 32 + ty + 8 * r, j = tj * 32 + tx;
+      if (i < K && j < K && j >= i) {
+        const double v = fixed_value(P[i * K + j], e0[i] + e0[j] + fix_scale);
+        G[i * ldg + j] = v;
+        tile[ty + 8 * r][tx] = v;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int64_t j = tj * 32 + ty + 8 * r, i = ti * 32 + tx;  // G[j][i] = G[i][j]
+      if (i < K && j < K && j >= i) G[j * ldg + i] = tile[tx][ty + 8 * r];
+    }
+    __syncthreads();
+  }
 }
 
 struct DevState {
@@ -537,6 +574,164 @@ int ozk_matmul_f64_multi(ozk_context* ctx, const double* const* A, const int64_t
   if (!gate) return OZK_OK;
   if ((rc = run_pass(ctx, a, false, 0))) return rc;
   return wait_all(ctx, s.data());
+}
+
+
+int ozk_gram_f64_multi(ozk_context* ctx, const double* const* A, const int64_t* lda, double* const* G,
+                       const int64_t* ldg, int64_t N, int64_t K, int n_hi, int n_lo, int flags,
+                       void* const* streams, int32_t* const* status_dev) {
+  if (!ctx) return set_error(OZK_ERR_ARG, "NULL context");
+  if (ctx->aborted) return set_error(OZK_ERR_NCCL, "the context was aborted after a failure");
+  if (!A || !lda || !G || !ldg) return set_error(OZK_ERR_ARG, "NULL pointer array");
+  if (N < 1 || K < 1) return set_error(OZK_ERR_ARG, "bad shape (N, K must be >= 1)");
+  if (n_hi < 1 || n_lo < 0 || n_hi > OZK_MAX_SIDE || n_lo > OZK_MAX_SIDE)
+    return set_error(OZK_ERR_ARG, "n_hi must be in [1,%d] and n_lo in [0,%d]", OZK_MAX_SIDE,
+                     OZK_MAX_SIDE);
+  const NcclApi& api = nccl();
+  const int P = ctx->nranks;
+  const int nl = (int)ctx->dev.size();
+  for (int i = 0; i < nl; ++i) {
+    const int64_t rows = rows_of(N, ctx->dev[i].rank, P);
+    if (rows > 0 && (!A[i] || lda[i] < K)) return set_error(OZK_ERR_ARG, "A[%d] / lda", i);
+    if (!G[i] || ldg[i] < K) return set_error(OZK_ERR_ARG, "G[%d] / ldg", i);
+  }
+  const int rho = ozk_compute_rho_f32(N);  // the contraction is over all N rows
+  int rc = check_bound(N, 24 - rho);
+  if (rc) return rc;
+  // int8 codes and the int8 GEMM's raw sums, decided from the global shapes
+  // (the same on every rank)
+  const int64_t rmax = (N + P - 1) / P;
+  const int64_t k8 = round_up(rmax > 0 ? rmax : 1, kS8KB);
+  cudaSetDevice(ctx->dev[0].device);
+  if (!(s8_enabled() && k8 <= 65536 &&
+        slice_gemm_s8_eligible(K, K, k8, OZK_ACC_FIXED, rho, gemm_state_bytes(ctx->dev[0].device))))
+    return set_error(OZK_ERR_UNSUPPORTED,
+                     "the multi-GPU gram needs int8 codes (rho >= %d: N > 4096), K >= 256 and at "
+                     "most 65536 rows per rank",
+                     kS8MinRho);
+  const int nS = n_hi + n_lo;
+  const int npass = n_hi > n_lo ? n_hi : n_lo;
+  uint8_t pa[OZK_MAX_PAIRS], pb[OZK_MAX_PAIRS];
+  const int np = ozk_pair_schedule_snake(n_hi, n_lo, pa, pb, OZK_MAX_PAIRS);
+  if (np < 0) return np;
+  std::vector<cudaStream_t> s(nl);
+  for (int i = 0; i < nl; ++i) s[i] = streams ? (cudaStream_t)streams[i] : nullptr;
+  struct Ws {
+    double* AT;    // [K][rows]: this rank's part of each line (column of A)
+    int8_t* S;     // [nS][K][k8] codes of the part
+    int32_t* e;    // [nS][K]
+    float* pmax;   // [2][K] this rank's maxima
+    float* gmax;   // [2][K] all ranks' maxima
+    long long* P;  // [K][K] int64 sums (upper triangle)
+    int32_t* flags_send;
+    int32_t* flags_all;
+    int32_t* gate;
+    double* state;
+    size_t state_bytes;
+  };
+  std::vector<Ws> ws(nl);
+  for (int i = 0; i < nl; ++i) {
+    DevState& d = ctx->dev[i];
+    cudaSetDevice(d.device);
+    const int64_t rows = rows_of(N, d.rank, P);
+    const size_t sb = gemm_state_bytes(d.device);
+    size_t off = 0;
+    auto take = [&](size_t n) { size_t o = off; off += a256(n); return o; };
+    const size_t oAT = take((size_t)K * (rows > 0 ? rows : 1) * 8), oS = take((size_t)nS * K * k8),
+                 oe = take((size_t)nS * K * 4), opm = take((size_t)2 * K * 4),
+                 ogm = take((size_t)2 * K * 4), oP = take((size_t)K * K * 8), ofs = take(8),
+                 ofa = take((size_t)8 * P), og = take(4), ost = take(sb);
+    if ((rc = grow(d, off))) return rc;
+    char* b = (char*)d.buf;
+    Ws& w = ws[i];
+    w.AT = (double*)(b + oAT);
+    w.S = (int8_t*)(b + oS);
+    w.e = (int32_t*)(b + oe);
+    w.pmax = (float*)(b + opm);
+    w.gmax = (float*)(b + ogm);
+    w.P = (long long*)(b + oP);
+    w.flags_send = (int32_t*)(b + ofs);
+    w.flags_all = (int32_t*)(b + ofa);
+    w.gate = (int32_t*)(b + og);
+    w.state = (double*)(b + ost);
+    w.state_bytes = sb;
+    cudaError_t e = cudaMemsetAsync(w.flags_send, 0, 8, s[i]);
+    if (e == cudaSuccess) e = cudaMemsetAsync(w.pmax, 0, (size_t)2 * K * 4, s[i]);
+    if (e != cudaSuccess) return set_cuda_error("cudaMemsetAsync", e);
+    // the rank's rows of A as lines (columns of A), then the split's maxima
+    if (rows > 0) {
+      if ((rc = launch_transpose_f64(A[i], lda[i], rows, K, w.AT, s[i]))) return rc;
+      if ((rc = launch_line_pass_s8(w.AT, rows, K, rows, -1, npass, rho, n_hi, n_lo, nullptr,
+                                    w.pmax, w.S, k8, w.e, w.flags_send + 1, w.flags_send, s[i])))
+        return rc;
+    }
+  }
+  // the slice passes: the lines' maxima over all ranks, then this rank's codes
+  for (int t = 0; t < npass; ++t) {
+    ncclResult_t nr = api.GroupStart();
+    for (int i = 0; i < nl && nr == ncclSuccess; ++i)
+      nr = api.AllReduce(ws[i].pmax, ws[i].gmax, (size_t)2 * K, ncclFloat32, ncclMax,
+                         ctx->dev[i].comm, s[i]);
+    ncclResult_t ge = api.GroupEnd();
+    if (nr != ncclSuccess) return nccl_error("all-reduce of the line maxima", nr);
+    if (ge != ncclSuccess) return nccl_error("ncclGroupEnd", ge);
+    for (int i = 0; i < nl; ++i) {
+      cudaSetDevice(ctx->dev[i].device);
+      const int64_t rows = rows_of(N, ctx->dev[i].rank, P);
+      Ws& w = ws[i];
+      if (rows > 0) {
+        rc = launch_line_pass_s8(w.AT, rows, K, rows, t, npass, rho, n_hi, n_lo, w.gmax, w.pmax,
+                                 w.S, k8, w.e, w.flags_send + 1, w.flags_send, s[i]);
+      } else {
+        // no rows here: zero codes; the exponents follow from gmax as anywhere
+        rc = launch_line_pass_s8(w.AT, 0, K, 0, t, npass, rho, n_hi, n_lo, w.gmax, w.pmax, w.S,
+                                 k8, w.e, w.flags_send + 1, w.flags_send, s[i]);
+      }
+      if (rc) return rc;
+    }
+  }
+  // every rank's flags; then the raw sums of this rank's rows (gated), their
+  // all-reduce, and the FP64 values with the mirror
+  ncclResult_t nr = api.GroupStart();
+  for (int i = 0; i < nl && nr == ncclSuccess; ++i)
+    nr = api.AllGather(ws[i].flags_send, ws[i].flags_all, 2, ncclInt32, ctx->dev[i].comm, s[i]);
+  ncclResult_t ge = api.GroupEnd();
+  if (nr != ncclSuccess) return nccl_error("all-gather of the flags", nr);
+  if (ge != ncclSuccess) return nccl_error("ncclGroupEnd", ge);
+  const bool nowait = (flags & OZK_MULTI_NOWAIT) != 0;
+  for (int i = 0; i < nl; ++i) {
+    cudaSetDevice(ctx->dev[i].device);
+    Ws& w = ws[i];
+    k_reduce_flags<<<1, 32, 0, s[i]>>>(w.flags_all, P, w.gate, status_dev ? status_dev[i] : nullptr,
+                                       OZK_FLAG_REDO);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemsetAsync(w.P, 0, (size_t)K * K * 8, s[i]);
+    if (e != cudaSuccess) return set_cuda_error("k_reduce_flags / memset", e);
+    const int64_t rows = rows_of(N, ctx->dev[i].rank, P);
+    if (rows > 0 &&
+        (rc = launch_slice_gemm_ex(w.S, w.e, nS, w.S, w.e, nS, K, K, k8, pa, pb, np, OZK_ACC_FIXED,
+                                   1, 1.0, 0.0, nullptr, 0, nullptr, K, nullptr, w.state,
+                                   w.state_bytes, rho, status_dev ? status_dev[i] : nullptr, true,
+                                   w.gate, 0, s[i], w.P)))
+      return rc;
+  }
+  nr = api.GroupStart();
+  for (int i = 0; i < nl && nr == ncclSuccess; ++i)
+    nr = api.AllReduce(ws[i].P, ws[i].P, (size_t)K * K, ncclInt64, ncclSum, ctx->dev[i].comm, s[i]);
+  ge = api.GroupEnd();
+  if (nr != ncclSuccess) return nccl_error("all-reduce of the sums", nr);
+  if (ge != ncclSuccess) return nccl_error("ncclGroupEnd", ge);
+  for (int i = 0; i < nl; ++i) {
+    cudaSetDevice(ctx->dev[i].device);
+    Ws& w = ws[i];
+    const int64_t tiles = ((K + 31) / 32) * ((K + 31) / 32);
+    const unsigned grid = (unsigned)(tiles < 65535 ? tiles : 65535);
+    k_gram_finalize<<<grid, 256, 0, s[i]>>>(w.P, K, w.e, 2 * (rho - 24) - kFixFrac, w.gate, G[i],
+                                            ldg[i]);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error("k_gram_finalize launch", e);
+  }
+  return nowait ? OZK_OK : wait_all(ctx, s.data());
 }
 
 }  // extern "C"

@@ -324,12 +324,40 @@ def residual_rowsharded(A_local, x, b_local, precision="high", accumulation="bf1
                     mode="ozaki")
 
 
-def gram_rowsharded(A_local, precision="high", group=None):
-    """This rank's block of rows of G = A^T A (gram(mode='ozaki')) with A's rows
-    split over the ranks.
+def _gram_reduced(lib, Ad, N, K, n_hi, n_lo, group):
+    """G = A^T A through ozk_gram_f64_multi (partial int64 Gram sums reduced over
+    the ranks).  Returns (G on this rank, OZK_FLAG_* bits of all ranks), or
+    None where the operator does not apply (the same decision on every rank)."""
+    ctx = context(group)
+    dev = Ad.device
+    G = torch.empty((K, K), dtype=torch.float64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    P, I64 = ctypes.c_void_p, ctypes.c_int64
+    rc = lib.ozk_gram_f64_multi(ctx.ptr, (P * 1)(Ad.data_ptr() if Ad.numel() else None),
+                                (I64 * 1)(K), (P * 1)(G.data_ptr()), (I64 * 1)(K), N, K, n_hi,
+                                n_lo, L.OZK_MULTI_NOWAIT, (P * 1)(D.stream_handle(dev)),
+                                (P * 1)(status.data_ptr()))
+    if rc == L.OZK_ERR_UNSUPPORTED:
+        return None
+    L.check(rc)
+    return G, int(status.item())
 
-    A_local: this rank's rows of A (CUDA float64, N_r x K).  Rank r owns columns
-    [rK/P, (r+1)K/P) of A and rows [rK/P, (r+1)K/P) of G:
+
+def gram_rowsharded(A_local, precision="high", group=None, full=False):
+    """This rank's block of rows of G = A^T A (gram(mode='ozaki')) with A's rows
+    split over the ranks (all of G with full=True).
+
+    With int8 slice codes (N > 4096, K >= 256) and A's rows on row_range(N, r, P),
+    this is ozk_gram_f64_multi, the reduction of partial Gram blocks: each slice
+    pass takes the lines' maxima over all ranks, each rank's int8 GEMM adds up
+    its rows' exact pair products in int64, the sums are all-reduced exactly and
+    rounded to FP64 once.  Each pair's term is rounded at 2^-36 of the top
+    product grid on each rank's part, so a rare element can differ from the
+    single-GPU gram in its last bit (bit-identical with one rank).
+
+    Otherwise (and if a slice has no exact int8 code on some rank) A's columns
+    travel instead.  Rank r owns columns [rK/P, (r+1)K/P) of A and rows
+    [rK/P, (r+1)K/P) of G:
       1. an all-to-all over NCCL gives each rank every row of its columns, so it
          extracts their slices (lines of length N) itself, as the single-GPU
          gram does;
@@ -361,6 +389,16 @@ def gram_rowsharded(A_local, precision="high", group=None):
     cols = [row_range(K, r, world) for r in range(world)]
     c0, c1 = cols[rank]
     kr = c1 - c0
+    if all(n == row_range(N, r, world)[1] - row_range(N, r, world)[0]
+           for r, n in enumerate(counts)):
+        got = _gram_reduced(lib, Ad, N, K, n_hi, n_lo, group)
+        if got is not None and not got[1] & L.OZK_FLAG_REDO:
+            Gf, flags = got
+            if flags & L.OZK_FLAG_TIMEOUT:
+                raise L.OzakiError(L.OZK_ERR_TIMEOUT, "a device-side wait exceeded its time budget")
+            if flags:
+                raise ValueError(_PREFIX + "; ".join(_flags_reasons(flags)))
+            return Gf if full else Gf[c0:c1]
     # 1. columns of A to their owners
     send = torch.cat([Ad[:, a:b].reshape(-1) for a, b in cols])
     recv = torch.empty(N * kr, dtype=torch.float64, device=dev)
@@ -437,4 +475,6 @@ def gram_rowsharded(A_local, precision="high", group=None):
         raise L.OzakiError(L.OZK_ERR_TIMEOUT, "a device-side wait exceeded its time budget")
     if flags:
         raise ValueError(_PREFIX + "; ".join(_flags_reasons(flags)))
+    if full:
+        return gather_rows(G, K, group=group)
     return G

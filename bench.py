@@ -828,9 +828,10 @@ def ours(args):
                              if world > 1 else
                              "ozk_matmul_f64 (the C-ABI operator, all its launches)")
                             if kind == "matmul" else (
-                                "gram_rowsharded: all-to-all of A's columns, local line "
-                                "extraction, all-gather of the slice stacks (NCCL), this rank's "
-                                "rows of G" if (kind == "gram" and world > 1) else
+                                "gram_rowsharded -> ozk_gram_f64_multi (the C-ABI multi-GPU "
+                                "operator): rows of A sharded, each slice pass's line maxima "
+                                "all-reduced (NCCL), partial int64 Gram sums all-reduced, one "
+                                "FP64 rounding" if (kind == "gram" and world > 1) else
                                 f"ozk_{kind}_f64 (the C-ABI operator)"
                                 + (" on each rank's rows (no collective)" if world > 1 else "")),
                    "inputs": ("each rank's rows of A (and b) from RandomState(1 + rank); "

@@ -1045,7 +1045,7 @@ int launch_slice_gemm_ex(const void* SA, const int32_t* eA, int nA, const void* 
     if (pair_a[p] >= nA || pair_b[p] >= nB) return set_error(OZK_ERR_ARG, "pair index out of range");
   if (mode != OZK_ACC_F64 && mode != OZK_ACC_PRODUCTS && mode != OZK_ACC_FIXED)
     return set_error(OZK_ERR_ARG, "bad mode");
-  if (mode != OZK_ACC_PRODUCTS && !C) return set_error(OZK_ERR_ARG, "C is NULL");
+  if (mode != OZK_ACC_PRODUCTS && !C && !C64) return set_error(OZK_ERR_ARG, "C is NULL");
   if (mode == OZK_ACC_FIXED && (rho < 1 || rho > 30))
     return set_error(OZK_ERR_ARG, "OZK_ACC_FIXED needs the extraction rho");
   if (mode == OZK_ACC_PRODUCTS && !products) return set_error(OZK_ERR_ARG, "products is NULL");

@@ -91,3 +91,31 @@ def test_without_int8_codes_unsupported(ctx):
     A = np.random.RandomState(2).randn(3000, 300)  # rho 18: BF16 slices
     rc, _, _ = gram_multi(ctx, A, 4, 1)
     assert rc == L.OZK_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("mode", [L.OZK_B_REPLICATED, L.OZK_B_ROOT, L.OZK_B_COLUMNS])
+@pytest.mark.parametrize("N,K,M", [(600, 5000, 300), (300, 700, 257)])
+def test_one_rank_matmul_multi_equals_single_gpu(ctx, mode, N, K, M):
+    """ozk_matmul_f64_multi on a one-rank context, every way of bringing B:
+    the single-GPU result (ozk_matmul_f64, fixed-point sums) bit for bit, for
+    int8 codes (K = 5000) and BF16 slices (K = 700), blocking and NOWAIT."""
+    lib = L.load()
+    rng = np.random.RandomState(N + K + M + mode)
+    A, B = rng.randn(N, K), rng.randn(K, M)
+    Ad, Bd = torch.as_tensor(A).cuda(), torch.as_tensor(B).cuda()
+    ref = torch.empty((N, M), dtype=torch.float64, device="cuda")
+    st0 = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    L.check(lib.ozk_matmul_f64(Ad.data_ptr(), K, Bd.data_ptr(), M, ref.data_ptr(), M, N, K, M, -1,
+                               4, 1, L.OZK_ACC_FIXED, None, 0, st0.data_ptr(), s))
+    P, I64 = ctypes.c_void_p, ctypes.c_int64
+    for flags in (0, L.OZK_MULTI_NOWAIT):
+        C = torch.full((N, M), float("nan"), dtype=torch.float64, device="cuda")
+        st = torch.zeros(1, dtype=torch.int32, device="cuda")
+        L.check(lib.ozk_matmul_f64_multi(
+            ctx, (P * 1)(Ad.data_ptr()), (I64 * 1)(K), (P * 1)(Bd.data_ptr()), (I64 * 1)(M),
+            (P * 1)(C.data_ptr()), (I64 * 1)(M), N, K, M, 4, 1, mode, flags, (P * 1)(s),
+            (P * 1)(st.data_ptr())))
+        torch.cuda.synchronize()
+        assert st.item() == 0 and st0.item() == 0
+        assert torch.equal(C.view(torch.int64), ref.view(torch.int64)), (mode, flags)

@@ -813,7 +813,7 @@ def ours(args):
         "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": op_ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
-        "data": "synthetic (np.random.RandomState(0), BASELINE's recipe)",
+        "data": "synthetic (seeded; config.inputs says how)",
         "config": {"workload": f"{name}: {desc} ({n_pairs} slice GEMMs), "
                                f"accumulation={'bf16_interleaved' if kind != 'matmul' else 'fused'}",
                    "N": n, "K": k, "M": m, "precision": precision, "rho": rho,

@@ -509,6 +509,49 @@ __device__ __forceinline__ bool tag_wait(const uint64_t* p, uint32_t rank, uint3
   }
 }
 
+// Relaxed 64-bit store into the shared memory of CTA `rank` of this cluster
+// (this CTA included) at the offset of the local object `p`: one
+// single-copy-atomic word, sent without waiting for it to land.
+__device__ __forceinline__ void st_dsmem_relaxed_u64(uint64_t* p, uint32_t rank, uint64_t v) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
+  asm volatile("st.relaxed.cluster.shared::cluster.b64 [%0], %1;" ::"r"(remote), "l"(v) : "memory");
+}
+
+// Bounded wait for a tagged word in this CTA's own shared memory, (tag << 32)
+// | value, which a peer CTA of the cluster stored with st_dsmem_relaxed_u64.
+// The poll is a local load, so waiting costs no round trip to the peer.
+// Returns like tag_wait.
+__device__ __forceinline__ bool tag_wait_local(const uint64_t* p, uint32_t tag, uint32_t& val,
+                                               volatile int* abort, int32_t* status,
+                                               uint64_t budget_ns) {
+  const uint32_t a = smem_u32(p);
+  uint64_t w;
+  asm volatile("ld.relaxed.cluster.shared::cta.b64 %0, [%1];" : "=l"(w) : "r"(a) : "memory");
+  if ((uint32_t)(w >> 32) == tag) {
+    val = (uint32_t)w;
+    return true;
+  }
+  val = 0;
+  if (*abort) return false;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    asm volatile("ld.relaxed.cluster.shared::cta.b64 %0, [%1];" : "=l"(w) : "r"(a) : "memory");
+    if ((uint32_t)(w >> 32) == tag) {
+      val = (uint32_t)w;
+      return true;
+    }
+    if ((i & 255) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > budget_ns) {
+        *abort = 1;
+        raise_flag(status, OZK_FLAG_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
 // Cluster barrier without memory ordering (arrive.relaxed): the data that
 // crosses it carries tags instead (tag_wait).
 __device__ __forceinline__ void cluster_sync_relaxed() {

@@ -328,12 +328,13 @@ __global__ void __launch_bounds__(kRegNT, 2) k_extract_rows_reg(
 // and after the barrier every warp reduces all partials of the line and
 // derives the slice parameters itself, then sweeps its registers, taking the
 // next pass's maxima on the way.  In a cluster each partial is one 64-bit word
-// (pass << 32) | FP32 bits, and a reader in any CTA of the cluster takes it
-// once the tag matches (a bounded spin), so the CTAs need no cluster barrier
-// per pass.  Two parity slots suffice: a warp posts its pass-g+1 partial only
-// after reading every pass-g partial, so no CTA can reach pass g+2, and
-// rewrite a slot, before every warp of every peer has read that slot's pass-g
-// value.  Slices are
+// (pass << 32) | FP32 bits, which the warp stores into the inbox of every CTA
+// of the cluster (remote stores, not waited for); a reader polls its own CTA's
+// inbox until the tag matches (a bounded spin), so the CTAs need no cluster
+// barrier per pass and no poll crosses the cluster.  Two parity slots
+// suffice: a warp posts its pass-g+1 partial only after reading every pass-g
+// partial, so no CTA can reach pass g+2, and rewrite a slot, before every warp
+// of every CTA has read that slot's pass-g value.  Slices are
 // written as 8-byte (BF16) or 4-byte (int8) words, all columns up to k_pad
 // included; int8 codes are staged in shared memory (two buffers per side), and
 // one thread bulk-stores a pass's codes after the next barrier, which takes
@@ -398,8 +399,9 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ uint64_t s_bar;
   __shared__ float s_part[2][2][NW];  // CL == 1: [parity][hi max, lo max][warp]
-  // CL > 1: [parity][hi, lo][warp], (pass << 32) | FP32 bits (lo: bit 31 = line flags)
-  __shared__ uint64_t s_tag[2][2][CL > 1 ? NW : 1];
+  // CL > 1: the inbox of every warp's partials in the cluster, [parity][hi, lo]
+  // [CTA rank * NW + warp], (pass << 32) | FP32 bits (lo: bit 31 = line flags)
+  __shared__ uint64_t s_tag[2][2][CL > 1 ? NP : 1];
   __shared__ int s_abort;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t crank = CL > 1 ? cluster_ctarank() : 0;
@@ -429,7 +431,7 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
     fence_mbar_init();
   }
   if constexpr (CL > 1)
-    if (tid < 4 * NW) (&s_tag[0][0][0])[tid] = ~0ull;  // no pass carries tag 0xffffffff
+    for (int i = tid; i < 4 * NP; i += NT) (&s_tag[0][0][0])[i] = ~0ull;  // no pass has tag ~0
   // the tagged slots are initialised before any peer reads them
   if constexpr (CL > 1) cluster_sync();
   else __syncthreads();
@@ -538,16 +540,18 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
       ml = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ml)));
       bool bad = t == 0 && line_bad;
       float gh = 0.0f, gl = 0.0f;
-      if (lane == 0) {
-        if constexpr (CL == 1) {
+      if constexpr (CL == 1) {
+        if (lane == 0) {
           s_part[par][0][warp] = mh;
           s_part[par][1][warp] = ml;
-        } else {
-          const uint64_t tag = (uint64_t)gpass << 32;
-          st_smem_relaxed_u64(&s_tag[par][0][warp], tag | __float_as_uint(mh));
-          st_smem_relaxed_u64(&s_tag[par][1][warp],
-                              tag | __float_as_uint(ml) | (bad ? 0x80000000u : 0u));
         }
+      } else if (lane < CL) {
+        // lane r sends the warp's partials to CTA r's inbox
+        const uint64_t tag = (uint64_t)gpass << 32;
+        const int slot = (int)crank * NW + warp;
+        st_dsmem_relaxed_u64(&s_tag[par][0][slot], lane, tag | __float_as_uint(mh));
+        st_dsmem_relaxed_u64(&s_tag[par][1][slot], lane,
+                             tag | __float_as_uint(ml) | (bad ? 0x80000000u : 0u));
       }
       if constexpr (STAGE) {
         fence_proxy_async_smem();            // this thread's staged codes, for the bulk store
@@ -573,10 +577,10 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
           const int e = e0 + lane;
           if (e < NP) {
             uint32_t vh, vl;
-            tag_wait(&s_tag[par][0][e % NW], (uint32_t)(e / NW), gpass, vh,
-                     (volatile int*)&s_abort, status, budget_ns);
-            tag_wait(&s_tag[par][1][e % NW], (uint32_t)(e / NW), gpass, vl,
-                     (volatile int*)&s_abort, status, budget_ns);
+            tag_wait_local(&s_tag[par][0][e], gpass, vh, (volatile int*)&s_abort, status,
+                           budget_ns);
+            tag_wait_local(&s_tag[par][1][e], gpass, vl, (volatile int*)&s_abort, status,
+                           budget_ns);
             gh = fmaxf(gh, __uint_as_float(vh));
             gl = fmaxf(gl, __uint_as_float(vl & 0x7fffffffu));
             bad = bad || (vl >> 31);
@@ -1288,14 +1292,15 @@ static int launch_rows_bulk_any(const double* X, int64_t ldx, int64_t rows, int6
   if (k_pad <= 12288)
     return launch_rows_bulk<512, 24, 1, S8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad, exps,
                                             status, s8_fail, gate, dev, stream);
-  // Longer rows: a cluster of CTAs per row, 8192 columns each (two CTAs of
-  // different rows per SM), line maxima exchanged through distributed shared
-  // memory.
+  // Longer rows: a cluster of CTAs per row, line maxima exchanged through
+  // distributed shared memory.  Up to 32768 columns, CTAs of 128 threads
+  // holding 4096 columns each (four CTAs of different rows per SM); longer,
+  // 256 threads and 8192 columns (two per SM), so the cluster stays at 8.
   if (k_pad <= 16384)
-    return launch_rows_bulk<256, 32, 2, S8, 2>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
+    return launch_rows_bulk<128, 32, 4, S8, 4>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
                                                exps, status, s8_fail, gate, dev, stream);
   if (k_pad <= 32768)
-    return launch_rows_bulk<256, 32, 2, S8, 4>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
+    return launch_rows_bulk<128, 32, 4, S8, 8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
                                                exps, status, s8_fail, gate, dev, stream);
   return launch_rows_bulk<256, 32, 2, S8, 8>(X, ldx, rows, K, rho, n_hi, n_lo, slices, k_pad,
                                              exps, status, s8_fail, gate, dev, stream);

@@ -292,6 +292,15 @@ int ozk_context_create_local(ozk_context** ctx, int ndev, const int* devices);
 int ozk_context_destroy(ozk_context* ctx);
 /* Global rank count, the global rank of the first local GPU, local GPU count. */
 int ozk_context_info(const ozk_context* ctx, int* nranks, int* first_rank, int* nlocal);
+/* Waits for the work that OZK_MULTI_NOWAIT calls enqueued on streams[i] (one
+ * per local GPU, NULL: the legacy default streams) with the bound of the
+ * blocking calls: NCCL's asynchronous errors are watched, and after
+ * OZK_NCCL_TIMEOUT_MS (default 300 s) or an NCCL failure the communicators are
+ * aborted, the context becomes unusable and OZK_ERR_TIMEOUT / OZK_ERR_NCCL is
+ * returned.  A rank whose peer failed (or never made its call) therefore gets
+ * an error instead of waiting forever, as a plain stream synchronisation
+ * would. */
+int ozk_context_wait(ozk_context* ctx, void* const* streams);
 
 /* How B reaches every rank in ozk_matmul_f64_multi. */
 #define OZK_B_REPLICATED 0 /* every rank holds all of B (K x M) and extracts it */

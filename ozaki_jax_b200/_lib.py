@@ -85,6 +85,7 @@ SIGNATURES = {
     "ozk_context_create_local": (c_int, [vp, c_int, vp]),
     "ozk_context_destroy": (c_int, [vp]),
     "ozk_context_info": (c_int, [vp, vp, vp, vp]),
+    "ozk_context_wait": (c_int, [vp, vp]),
     "ozk_matmul_f64_multi": (c_int, [vp, vp, vp, vp, vp, vp, vp, c_i64, c_i64, c_i64, c_int,
                                      c_int, c_int, c_int, vp, vp]),
     "ozk_gram_f64_multi": (c_int, [vp, vp, vp, vp, vp, c_i64, c_i64, c_int, c_int, c_int, vp,

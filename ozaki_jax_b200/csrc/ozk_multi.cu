@@ -270,7 +270,8 @@ uint64_t multi_timeout_ms() {
 
 // Waits for every local stream with a deadline, watching NCCL for
 // asynchronous errors; on a failure or at the deadline every communicator of
-// the context is aborted (the context is unusable afterwards).
+// the context is aborted (the context is unusable afterwards).  The first
+// 2 ms poll without sleeping, so a short step pays no sleep granularity.
 int wait_all(ozk_context* ctx, cudaStream_t* s) {
   const auto t0 = std::chrono::steady_clock::now();
   const uint64_t budget = multi_timeout_ms();
@@ -297,7 +298,8 @@ int wait_all(ozk_context* ctx, cudaStream_t* s) {
                          "context was aborted",
                          (unsigned long long)budget);
       }
-      std::this_thread::sleep_for(std::chrono::microseconds(50));
+      if (ms < 2) std::this_thread::yield();
+      else std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
   }
   return OZK_OK;
@@ -502,6 +504,15 @@ int ozk_context_destroy(ozk_context* ctx) {
   }
   delete ctx;
   return rc;
+}
+
+int ozk_context_wait(ozk_context* ctx, void* const* streams) {
+  if (!ctx) return set_error(OZK_ERR_ARG, "NULL context");
+  if (ctx->aborted) return set_error(OZK_ERR_NCCL, "the context was aborted after a failure");
+  if (!nccl().ok) return set_error(OZK_ERR_NCCL, "%s", nccl().why);
+  std::vector<cudaStream_t> s(ctx->dev.size());
+  for (size_t i = 0; i < s.size(); ++i) s[i] = streams ? (cudaStream_t)streams[i] : nullptr;
+  return wait_all(ctx, s.data());
 }
 
 int ozk_context_info(const ozk_context* ctx, int* nranks, int* first_rank, int* nlocal) {

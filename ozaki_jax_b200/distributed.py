@@ -129,6 +129,13 @@ class MultiContext:
         L.check(lib.ozk_context_create_rank(ctypes.byref(self.ptr), self.world, self.rank, idbuf,
                                             L.OZK_NCCL_ID_BYTES, self.device))
 
+    def wait(self, dev):
+        """Bounded wait for the work NOWAIT calls enqueued on the current stream
+        of `dev` (ozk_context_wait): raises OzakiError (OZK_ERR_TIMEOUT or
+        OZK_ERR_NCCL, the context then unusable) where a peer failed."""
+        L.check(L.load().ozk_context_wait(
+            self.ptr, (ctypes.c_void_p * 1)(D.stream_handle(dev))))
+
     def close(self):
         if self.ptr:
             L.check(L.load().ozk_context_destroy(self.ptr))
@@ -237,6 +244,8 @@ def matmul_rowsharded(A_local, B, precision="high", b_source="replicated", group
             (I64 * 1)(Bd.shape[1] if Bd is not None else 0), (P * 1)(C.data_ptr()), (I64 * 1)(M),
             N, K, M, n_hi, n_lo, _B_MODES[b_source], flags, (P * 1)(D.stream_handle(dev)),
             (P * 1)(status.data_ptr())))
+        # a bounded wait: a peer that failed ends it with an error, not a hang
+        ctx.wait(dev)
 
     call(L.OZK_MULTI_NOWAIT)
     flags = int(status.item())  # the OZK_FLAG_* bits of every rank
@@ -340,6 +349,7 @@ def _gram_reduced(lib, Ad, N, K, n_hi, n_lo, group):
     if rc == L.OZK_ERR_UNSUPPORTED:
         return None
     L.check(rc)
+    ctx.wait(dev)
     return G, int(status.item())
 
 

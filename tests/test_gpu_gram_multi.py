@@ -98,7 +98,8 @@ def test_without_int8_codes_unsupported(ctx):
 def test_one_rank_matmul_multi_equals_single_gpu(ctx, mode, N, K, M):
     """ozk_matmul_f64_multi on a one-rank context, every way of bringing B:
     the single-GPU result (ozk_matmul_f64, fixed-point sums) bit for bit, for
-    int8 codes (K = 5000) and BF16 slices (K = 700), blocking and NOWAIT."""
+    int8 codes (K = 5000) and BF16 slices (K = 700), blocking and NOWAIT (then
+    ozk_context_wait)."""
     lib = L.load()
     rng = np.random.RandomState(N + K + M + mode)
     A, B = rng.randn(N, K), rng.randn(K, M)
@@ -116,6 +117,8 @@ def test_one_rank_matmul_multi_equals_single_gpu(ctx, mode, N, K, M):
             ctx, (P * 1)(Ad.data_ptr()), (I64 * 1)(K), (P * 1)(Bd.data_ptr()), (I64 * 1)(M),
             (P * 1)(C.data_ptr()), (I64 * 1)(M), N, K, M, 4, 1, mode, flags, (P * 1)(s),
             (P * 1)(st.data_ptr())))
+        # the bounded wait of NOWAIT calls (a no-op after a blocking one)
+        L.check(lib.ozk_context_wait(ctx, (P * 1)(s)))
         torch.cuda.synchronize()
         assert st.item() == 0 and st0.item() == 0
         assert torch.equal(C.view(torch.int64), ref.view(torch.int64)), (mode, flags)

@@ -131,6 +131,22 @@ def test_every_entry_point_checks_arguments_before_device_work():
     pb = (ctypes.c_uint8 * 4)()
     assert lib.ozk_triangular_schedule(0, pa, pb, 4) == ARG
     assert lib.ozk_triangular_schedule(8, pa, pb, 4) == ARG  # 36 pairs do not fit in 4
+    # the multi-GPU context and operators: a NULL context or bad arguments are
+    # refused before NCCL or CUDA is touched
+    vp1 = (ctypes.c_void_p * 1)(p)
+    i1 = (ctypes.c_int64 * 1)(4)
+    assert lib.ozk_nccl_unique_id(None, 0) == ARG
+    assert lib.ozk_context_create_rank(None, 2, 0, p, _lib.OZK_NCCL_ID_BYTES, 0) == ARG
+    out = ctypes.c_void_p()
+    assert lib.ozk_context_create_rank(ctypes.byref(out), 2, 2, p, _lib.OZK_NCCL_ID_BYTES,
+                                       0) == ARG
+    assert lib.ozk_context_create_local(ctypes.byref(out), 0, None) == ARG
+    assert lib.ozk_context_info(None, None, None, None) == ARG
+    assert lib.ozk_context_wait(None, None) == ARG
+    assert lib.ozk_context_destroy(None) == OK
+    assert lib.ozk_matmul_f64_multi(None, vp1, i1, vp1, i1, vp1, i1, 4, 4, 4, 4, 1,
+                                    _lib.OZK_B_REPLICATED, 0, None, None) == ARG
+    assert lib.ozk_gram_f64_multi(None, vp1, i1, vp1, i1, 4, 4, 4, 1, 0, None, None) == ARG
     # every refusal leaves a readable detail and a name for its code
     assert _lib.detail()
     for code in (ARG, UNSAFE, WS):

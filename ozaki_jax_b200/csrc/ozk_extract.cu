@@ -29,11 +29,13 @@ namespace ozk {
 __constant__ uint32_t c_log2_thr[OZK_LOG2_TABLE_LEN];
 __constant__ unsigned long long c_log2_thr64[OZK_LOG2_TABLE64_LEN];
 
-// floor(RN64(log2 m)) for finite m > 0 (ozaki_jax/extract.py:37, :82).
+// floor(RN64(log2 m)) for finite m > 0 (ozaki_jax/extract.py:37, :82); an
+// infinite or NaN m (a flagged line) gives 1024 without reading past the table.
 __device__ __forceinline__ int floor_log2_rn64(double m) {
   unsigned long long b = (unsigned long long)__double_as_longlong(m);
   int ex = (int)(b >> 52);
   int e = ex > 0 ? ex - 1023 : -1074 + (63 - __clzll((long long)b));
+  if (e > 1023) return 1024;
   return e + (b >= c_log2_thr64[e + 1074] ? 1 : 0);
 }
 
@@ -611,9 +613,8 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
       for (int side = 0; side < 2; ++side) {
         if (side == 0 ? !do_hi : !do_lo) continue;
         const float sg = side == 0 ? sh : sl, iv = side == 0 ? ih : il;
-        const uint32_t sg_bits = __float_as_uint(sg);
         const float2 sg2 = make_float2(sg, sg), nsg2 = make_float2(-sg, -sg);
-        const float2 iv2 = make_float2(iv, iv);
+        const float2 iv2 = make_float2(iv, iv), neg1 = make_float2(-1.0f, -1.0f);
         uint8_t* out;
         if constexpr (STAGE)
           out = s_code + (2 * par + side) * kCodeBytes + 4 * tid;
@@ -630,11 +631,14 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
             float2& r = side == 0 ? rh[2 * q + j] : rl[2 * q + j];
             const float2 tt = __fadd2_rn(r, sg2);   // RN(r + sigma)
             const float2 v = __fadd2_rn(tt, nsg2);  // the slice value, exact
-            r = __fadd2_rn(r, make_float2(-v.x, -v.y));  // exact
+            r = __ffma2_rn(v, neg1, r);             // r - v, exact
             mnext = max3_abs(mnext, r.x, r.y);
-            if constexpr (S8) {  // the int8 codes
-              u[2 * j] = __float_as_uint(tt.x) - sg_bits;
-              u[2 * j + 1] = __float_as_uint(tt.y) - sg_bits;
+            if constexpr (S8) {
+              // the int8 code bits(t) - bits(sigma) fits in a byte, and sigma =
+              // 0.75 * 2^(rho+c) has the mantissa 0x400000, whose low byte is
+              // 0: so the code is the low byte of bits(t) itself
+              u[2 * j] = __float_as_uint(tt.x);
+              u[2 * j + 1] = __float_as_uint(tt.y);
             } else {  // BF16 in the top halves
               const float2 b = __fmul2_rn(v, iv2);
               u[2 * j] = __float_as_uint(b.x);

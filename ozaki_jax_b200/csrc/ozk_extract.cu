@@ -371,13 +371,13 @@ __device__ __forceinline__ float max3_abs(float m, float a, float b) {
   return d;
 }
 
-// max(|a|, |b|), NaN if either is NaN (a NaN must not hide behind its
-// finite neighbour in a packed pair).
-__device__ __forceinline__ float max_abs_nan(float a, float b) {
+// max(m, |a|, |b|), NaN if any operand is NaN.
+__device__ __forceinline__ float max3_abs_nan(float m, float a, float b) {
   float d;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(fabsf(a)), "f"(fabsf(b)));
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(m), "f"(fabsf(a)), "f"(fabsf(b)));
   return d;
 }
+
 
 // PRESET = 16 n_hi + n_lo fixes the slice counts at compile time (the pass
 // loop unrolls, the lo residuals die after their last pass); 0 takes them
@@ -482,7 +482,6 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
     // residuals in pairs of adjacent columns, for the packed FP32 arithmetic
     float2 rh[EPT / 2], rl[EPT / 2];
     float mh = 0.0f, ml = 0.0f;
-    bool odd = false;  // a non-finite split value: the input is non-finite or beyond FP32
 #pragma unroll
     for (int q = 0; q < NG; ++q) {
       const int64_t k = 4 * ((int64_t)q * NT + tid);  // within this CTA's columns
@@ -502,11 +501,14 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
         float2& lo = rl[2 * q + j];
         split_f64(x[2 * j], hi.x, lo.x);
         split_f64(x[2 * j + 1], hi.y, lo.y);
-        odd |= !(max_abs_nan(hi.x, hi.y) <= 3.402823466e38f);
-        mh = max3_abs(mh, hi.x, hi.y);
+        mh = max3_abs_nan(mh, hi.x, hi.y);  // keeps a NaN, so the check below sees it
         ml = max3_abs(ml, lo.x, lo.y);
       }
     }
+    // a non-finite split value: the input is non-finite or beyond FP32.  Such a
+    // line is flagged below; its maxima (NaN or inf) give it garbage slices,
+    // which the flag keeps from being used.
+    const bool odd = !(mh <= 3.402823466e38f);
     int32_t flags = 0;
     if (odd) {  // rare: tell non-finite input from FP32 overflow
 #pragma unroll
@@ -536,8 +538,9 @@ __global__ void __launch_bounds__(NT, MINB) k_extract_rows_bulk(
       const bool do_hi = t < n_hi, do_lo = t < n_lo;
       // Partial line maxima of each warp (and, in the first pass, the line's
       // input flags), one barrier, then the line maxima in every warp.  The
-      // maxima are >= 0 and never NaN (max3_abs skips NaN operands), so their
-      // bit patterns order as unsigned integers: one redux per reduction.
+      // maxima are >= 0, so their bit patterns order as unsigned integers (a
+      // NaN, only in a line already flagged, is the positive canonical NaN):
+      // one redux per reduction.
       mh = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mh)));
       ml = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(ml)));
       bool bad = t == 0 && line_bad;

@@ -45,14 +45,12 @@ __device__ __forceinline__ long long fixed_term(uint32_t u, int t_off) {
 // product of the corresponding BF16 slices bit for bit (the same real number,
 // rounded the same way).
 __device__ __forceinline__ long long fixed_term_s32(int32_t P, int T) {
+  // T >= 0 (the common case): P * 2^T exactly; a two's-complement shift of P
+  // gives the same 64 bits as shifting |P| and restoring the sign
+  if (T >= 0) return (long long)((unsigned long long)(long long)P << min(T, 40));
   const unsigned long long a = (unsigned long long)(P < 0 ? -(long long)P : (long long)P);
-  unsigned long long v;
-  if (T >= 0) {
-    v = a << min(T, 40);
-  } else {
-    const int R = min(-T, 40);
-    v = (a + (1ull << (R - 1))) >> R;
-  }
+  const int R = min(-T, 40);
+  const unsigned long long v = (a + (1ull << (R - 1))) >> R;
   const long long sg = (long long)(P >> 31);  // 0 or -1
   return ((long long)v ^ sg) - sg;
 }

@@ -114,6 +114,35 @@ def test_column_codes_against_oracle_strided(K, ldx):
     assert np.array_equal(exps.cpu().numpy(), np.stack(list(eh) + list(el)).astype(np.int32))
 
 
+@pytest.mark.parametrize("K,lines,n_hi,n_lo", [(16400, 400, 4, 1), (20000, 300, 3, 1),
+                                               (32768, 300, 4, 1), (65536, 150, 4, 1),
+                                               (24000, 160, 5, 4)])
+def test_long_row_codes_against_oracle(K, lines, n_hi, n_lo):
+    """int8 row codes of rows that a cluster of CTAs holds together (clusters
+    of 4096- or 8192-column CTAs exchanging line maxima), with more rows than
+    resident clusters, so each cluster goes through several rows and the
+    exchange's tags and parity slots are reused: codes and exponents against
+    the oracle's row extraction on every row.  Rows of very different scales,
+    a zero row; 16400 columns leave three CTAs of each cluster without
+    columns."""
+    rng = np.random.RandomState(K + lines)
+    X = rng.randn(lines, K) * np.exp(rng.randn(lines, 1) * 8)
+    X *= np.exp(rng.randn(lines, K))
+    X[lines // 3] = 0.0  # a zero row
+    rho = O.compute_rho_f32(K)
+    codes, k8, exps, fail = s8_slices(X, rho, n_hi, n_lo, 1)
+    assert fail == 0
+    hi, lo = O.double_f32_split(X)
+    sh, eh = O.extract_rows_f32(hi, rho, n_hi)
+    sl, el = O.extract_rows_f32(lo, rho, n_lo)
+    q = codes.cpu().numpy()
+    for t, ref in enumerate(list(sh) + list(sl)):
+        assert np.array_equal(q[t, :, :K].astype(np.float64),
+                              np.asarray(ref, dtype=np.float64) * 2.0 ** (24 - rho)), t
+    assert np.all(q[:, :, K:] == 0)
+    assert np.array_equal(exps.cpu().numpy(), np.stack(list(eh) + list(el)).astype(np.int32))
+
+
 @pytest.mark.parametrize("K,lines,n_hi,n_lo", [(6001, 301, 4, 1), (8192, 3, 3, 1),
                                                (4500, 1, 4, 2), (7000, 600, 4, 1)])
 def test_column_codes_odd_counts(K, lines, n_hi, n_lo):

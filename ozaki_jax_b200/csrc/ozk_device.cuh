@@ -33,11 +33,13 @@ __device__ __forceinline__ double pow2d(int n) {
 // floor(RN32(log2(m))) for finite m > 0, from the per-binade threshold table
 // (thr[e + 149] = bits of the smallest m of binade e whose rounded log2 is e+1,
 // e in [-149, 127]).  An infinite or NaN m (a line the caller flags as
-// non-finite) gives 128 without reading past the table.
+// non-finite) gives 128, and m = 0 (which callers treat as a zero line
+// before asking) -150, without reading outside the table.
 __device__ __forceinline__ int floor_log2_rn32(float m, const uint32_t* thr) {
   uint32_t b = __float_as_uint(m);
   int e = (b >= 0x00800000u) ? (int)(b >> 23) - 127 : -149 + (31 - __clz(b));
   if (e > 127) return 128;
+  if (e < -149) return -150;
   return e + (b >= thr[e + 149] ? 1 : 0);
 }
 

@@ -30,12 +30,14 @@ __constant__ uint32_t c_log2_thr[OZK_LOG2_TABLE_LEN];
 __constant__ unsigned long long c_log2_thr64[OZK_LOG2_TABLE64_LEN];
 
 // floor(RN64(log2 m)) for finite m > 0 (ozaki_jax/extract.py:37, :82); an
-// infinite or NaN m (a flagged line) gives 1024 without reading past the table.
+// infinite or NaN m (a flagged line) gives 1024, and m = 0 (a zero line,
+// which callers handle before asking) -1075, without reading outside the table.
 __device__ __forceinline__ int floor_log2_rn64(double m) {
   unsigned long long b = (unsigned long long)__double_as_longlong(m);
   int ex = (int)(b >> 52);
   int e = ex > 0 ? ex - 1023 : -1074 + (63 - __clzll((long long)b));
   if (e > 1023) return 1024;
+  if (e < -1074) return -1075;
   return e + (b >= c_log2_thr64[e + 1074] ? 1 : 0);
 }
 

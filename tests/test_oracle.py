@@ -109,3 +109,31 @@ def test_exact_product_reference():
     # BLAS FP64 is within a few ulps of the correctly rounded product
     assert O.rel_err(A @ B, E) < 1e-15
     assert O.rel_err(O.host_numpy(A, B), E) < 1e-14
+
+
+def test_int8_code_is_the_low_byte_of_the_sum():
+    """The identity the device extraction uses for its int8 codes, checked in
+    NumPy float32 (IEEE round to nearest even): for rho >= 19 and every slice
+    exponent c in [-127, 127 - rho], sigma = 0.75 * 2^(rho+c) has a zero low
+    byte, and for a residual |r| < 2^(c+1) the code bits(RN(r + sigma)) -
+    bits(sigma) lies in [-2^(25-rho), 2^(25-rho)], equals the low byte of
+    bits(RN(r + sigma)) read as int8, and times 2^(rho+c-24) is the slice value
+    RN(RN(r + sigma) - sigma) of the reference's recurrence
+    (ozaki_jax/extract.py:116-154)."""
+    rng = np.random.RandomState(5)
+    for rho in range(19, 25):
+        for c in range(-127, 128 - rho):
+            sig = np.float32(0.75 * 2.0 ** (rho + c))
+            sb = int(sig.view(np.uint32))
+            assert sb & 0xFF == 0
+            r = (rng.uniform(-1.0, 1.0, 64) * 2.0 ** (c + 1)).astype(np.float32)
+            r = r[np.abs(r.astype(np.float64)) < 2.0 ** (c + 1)]
+            r = np.concatenate([r, np.float32([0.0, -0.0])])
+            t = (r + sig).astype(np.float32)
+            tb = t.view(np.uint32).astype(np.int64)
+            code = tb - sb
+            assert np.all(np.abs(code) <= 2 ** (25 - rho)), (rho, c)
+            low = (tb & 0xFF).astype(np.uint8).view(np.int8).astype(np.int64)
+            assert np.array_equal(low, code), (rho, c)
+            v = (t - sig).astype(np.float32)
+            assert np.array_equal(v.astype(np.float64), code * 2.0 ** (rho + c - 24)), (rho, c)

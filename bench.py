@@ -247,6 +247,13 @@ WORKLOADS = {
 }
 
 
+def workload_config(name, desc, n_pairs, kind, n, k, m, precision, rho, inputs):
+    """The part of `config` that names the workload, the same on both arms."""
+    return {"workload": f"{name}: {desc} ({n_pairs} slice GEMMs), "
+                        f"accumulation={'bf16_interleaved' if kind != 'matmul' else 'fused'}",
+            "N": n, "K": k, "M": m, "precision": precision, "rho": rho, "inputs": inputs}
+
+
 def make_inputs(n, k, m):
     """c2 (and --size): A (n x k) then B (k x m), i.i.d. N(0,1) from RandomState(0)."""
     rng = np.random.RandomState(0)
@@ -446,10 +453,12 @@ def reference_arm(args):
         "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
-        "data": "synthetic", "impl": "reference",
-        "config": {"workload": f"matmul {n}x{k}x{m} pipeline=ondevice accumulation=fused "
-                               f"precision={args.precision}",
-                   "N": n, "K": k, "M": m, "precision": args.precision},
+        "data": "synthetic (seeded; config.inputs says how)", "impl": "reference",
+        "config": dict(workload_config(
+            "c2", f"matmul {n}^3 precision={args.precision}, N(0,1)",
+            n_hi * n_hi + 2 * n_hi * n_lo, "matmul", n, k, m, args.precision,
+            O.compute_rho_f32(k), "RandomState(0), BASELINE's recipe"),
+            parallelism="host cores (the reference's CPU path)"),
         "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                          "sample": f"one step = the block C[0:{side}, 0:{side}] (A[0:{side}] x "
                                    f"B[:, 0:{side}], K={k}) by the NumPy port of matmul_numpy"
@@ -814,9 +823,11 @@ def ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": op_ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded; config.inputs says how)",
-        "config": {"workload": f"{name}: {desc} ({n_pairs} slice GEMMs), "
-                               f"accumulation={'bf16_interleaved' if kind != 'matmul' else 'fused'}",
-                   "N": n, "K": k, "M": m, "precision": precision, "rho": rho,
+        "config": {**workload_config(
+                       name, desc, n_pairs, kind, n, k, m, precision, rho,
+                       ("each rank's rows of A (and b) from RandomState(1 + rank); "
+                        "B / x from RandomState(0)") if "n_total" in W else
+                       "RandomState(0), BASELINE's recipe"),
                    "slices": "int8 codes" if s8 else "bf16",
                    "parallelism": f"row-blocks x{world}" if world > 1 else "1 GPU",
                    "timed": (f"ozk_matmul_f64_multi (the C-ABI multi-GPU operator), "
@@ -834,9 +845,6 @@ def ours(args):
                                 "FP64 rounding" if (kind == "gram" and world > 1) else
                                 f"ozk_{kind}_f64 (the C-ABI operator)"
                                 + (" on each rank's rows (no collective)" if world > 1 else "")),
-                   "inputs": ("each rank's rows of A (and b) from RandomState(1 + rank); "
-                              "B / x from RandomState(0)") if "n_total" in W else
-                             "RandomState(0), BASELINE's recipe",
                    "l2": "inputs larger than L2 (126 MB), no flush",
                    "l2_persisting_mb_after": round(l2_prev.value / 2**20, 1)},
         "parity": parity,
